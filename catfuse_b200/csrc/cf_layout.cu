@@ -1,0 +1,217 @@
+// cf_layout.cu — layout conversions between the reference layout
+// [T][B][C][H][W] and the fused path's pixel-major/time-inner layout
+// [B][H][W][T][C], weight packing, and the classifier head (global average
+// pool + fc).  All transposes go through a 32x33 shared tile so that both the
+// read and the write side are coalesced.
+#include "cf_common.cuh"
+
+namespace cf {
+namespace {
+
+constexpr int TB = 32;
+
+__device__ __forceinline__ float ld_f(const void* p, int fmt, int64_t i) {
+  return fmt == CF_FMT_F32 ? static_cast<const float*>(p)[i]
+                           : __half2float(static_cast<const __half*>(p)[i]);
+}
+
+// x[T][B][C][H][W] -> y[B][H][W][T][Cp].  grid: (ceil(W/32), ceil(Cp/32), T*B*H)
+__global__ void pack_kernel(const void* __restrict__ x, int fmt, __half* __restrict__ y, int T,
+                            int B, int C, int H, int W, int Cp) {
+  __shared__ float tile[TB][TB + 1];
+  const int w0 = blockIdx.x * TB, c0 = blockIdx.y * TB;
+  int z = blockIdx.z;
+  const int h = z % H; z /= H;
+  const int b = z % B;
+  const int t = z / B;
+  // read: threadIdx.x along w, threadIdx.y along c
+  for (int cy = threadIdx.y; cy < TB; cy += blockDim.y) {
+    const int c = c0 + cy, w = w0 + threadIdx.x;
+    float v = 0.f;
+    if (c < C && w < W) v = ld_f(x, fmt, ((((int64_t)t * B + b) * C + c) * H + h) * W + w);
+    tile[cy][threadIdx.x] = v;
+  }
+  __syncthreads();
+  // write: threadIdx.x along c
+  for (int wy = threadIdx.y; wy < TB; wy += blockDim.y) {
+    const int w = w0 + wy, c = c0 + threadIdx.x;
+    if (w < W && c < Cp)
+      y[((((int64_t)b * H + h) * W + w) * T + t) * Cp + c] = __float2half_rn(tile[threadIdx.x][wy]);
+  }
+}
+
+// y[B][H][W][T][C] -> x[T][B][C][H][W].  grid: (ceil(W/32), ceil(C/32), T*B*H)
+__global__ void unpack_kernel(const __half* __restrict__ y, void* __restrict__ x, int fmt, int T,
+                              int B, int C, int H, int W) {
+  __shared__ float tile[TB][TB + 1];
+  const int w0 = blockIdx.x * TB, c0 = blockIdx.y * TB;
+  int z = blockIdx.z;
+  const int h = z % H; z /= H;
+  const int b = z % B;
+  const int t = z / B;
+  for (int wy = threadIdx.y; wy < TB; wy += blockDim.y) {
+    const int w = w0 + wy, c = c0 + threadIdx.x;
+    float v = 0.f;
+    if (w < W && c < C) v = __half2float(y[((((int64_t)b * H + h) * W + w) * T + t) * C + c]);
+    tile[wy][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int cy = threadIdx.y; cy < TB; cy += blockDim.y) {
+    const int c = c0 + cy, w = w0 + threadIdx.x;
+    if (c < C && w < W) {
+      const int64_t i = ((((int64_t)t * B + b) * C + c) * H + h) * W + w;
+      if (fmt == CF_FMT_F32) static_cast<float*>(x)[i] = tile[threadIdx.x][cy];
+      else static_cast<__half*>(x)[i] = __float2half_rn(tile[threadIdx.x][cy]);
+    }
+  }
+}
+
+// v[B][C][HW] <-> v[B][HW][C].  grid: (ceil(HW/32), ceil(C/32), B)
+__global__ void v_layout_kernel(const float* __restrict__ src, float* __restrict__ dst, int C,
+                                int HW, int to_nhwc) {
+  __shared__ float tile[TB][TB + 1];
+  const int p0 = blockIdx.x * TB, c0 = blockIdx.y * TB;
+  const int64_t b = blockIdx.z;
+  const int64_t off = b * (int64_t)C * HW;
+  if (to_nhwc) {
+    for (int cy = threadIdx.y; cy < TB; cy += blockDim.y) {
+      const int c = c0 + cy, p = p0 + threadIdx.x;
+      if (c < C && p < HW) tile[cy][threadIdx.x] = src[off + (int64_t)c * HW + p];
+    }
+    __syncthreads();
+    for (int py = threadIdx.y; py < TB; py += blockDim.y) {
+      const int p = p0 + py, c = c0 + threadIdx.x;
+      if (p < HW && c < C) dst[off + (int64_t)p * C + c] = tile[threadIdx.x][py];
+    }
+  } else {
+    for (int py = threadIdx.y; py < TB; py += blockDim.y) {
+      const int p = p0 + py, c = c0 + threadIdx.x;
+      if (p < HW && c < C) tile[py][threadIdx.x] = src[off + (int64_t)p * C + c];
+    }
+    __syncthreads();
+    for (int cy = threadIdx.y; cy < TB; cy += blockDim.y) {
+      const int c = c0 + cy, p = p0 + threadIdx.x;
+      if (c < C && p < HW) dst[off + (int64_t)c * HW + p] = tile[threadIdx.x][cy];
+    }
+  }
+}
+
+__global__ void pack_weight_kernel(const float* __restrict__ w, __half* __restrict__ wp, int Cout,
+                                   int Cin, int KH, int KW, int Cin_p) {
+  const int64_t n = (int64_t)Cout * KH * KW * Cin_p;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int ci = (int)(i % Cin_p);
+    int64_t r = i / Cin_p;
+    const int kw = (int)(r % KW); r /= KW;
+    const int kh = (int)(r % KH);
+    const int co = (int)(r / KH);
+    float v = 0.f;
+    if (ci < Cin) v = w[(((int64_t)co * Cin + ci) * KH + kh) * KW + kw];
+    wp[i] = __float2half_rn(v);
+  }
+}
+
+// One CTA per (t, b): mean over H*W of x[b][:, :, t, :] into shared memory,
+// then one warp per class computes the fc dot product.
+__global__ void avgpool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
+                                  const float* __restrict__ fc_b, float* __restrict__ logits,
+                                  int T, int B, int HW, int C, int K) {
+  extern __shared__ float s_mean[];
+  const int t = blockIdx.x % T;
+  const int b = blockIdx.x / T;
+  const float inv = 1.0f / (float)HW;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float s = 0.f;
+    const __half* p = x + (((int64_t)b * HW) * T + t) * C + c;
+    for (int i = 0; i < HW; ++i) s += __half2float(p[(int64_t)i * T * C]);
+    s_mean[c] = s * inv;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int k = warp; k < K; k += blockDim.x >> 5) {
+    float acc = 0.f;
+    for (int c = lane; c < C; c += 32) acc += s_mean[c] * fc_w[(int64_t)k * C + c];
+    for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) logits[((int64_t)t * B + b) * K + k] = acc + (fc_b ? fc_b[k] : 0.f);
+  }
+}
+
+}  // namespace
+}  // namespace cf
+
+using namespace cf;
+
+extern "C" {
+
+int cf_pack_tbchw(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C, int64_t H,
+                  int64_t W, int64_t Cp, void* stream) {
+  if (!x || !y) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (x_fmt != CF_FMT_F32 && x_fmt != CF_FMT_F16) return fail(CF_ERR_INVALID_ARG, "bad x_fmt");
+  if (T < 0 || B < 0 || C <= 0 || H <= 0 || W <= 0 || Cp < C || Cp % 16)
+    return fail(CF_ERR_INVALID_ARG, "bad pack shape (Cp >= C, Cp %% 16 == 0)");
+  if (T * B == 0) return CF_OK;
+  if (T * B * H > 0x7FFFFFFF) return fail(CF_ERR_UNSUPPORTED, "T*B*H too large");
+  if (int rc = require_sm100()) return rc;
+  dim3 grid((unsigned)((W + TB - 1) / TB), (unsigned)((Cp + TB - 1) / TB), (unsigned)(T * B * H));
+  pack_kernel<<<grid, dim3(TB, 8), 0, static_cast<cudaStream_t>(stream)>>>(
+      x, x_fmt, static_cast<__half*>(y), (int)T, (int)B, (int)C, (int)H, (int)W, (int)Cp);
+  return check_launch("pack launch");
+}
+
+int cf_unpack_bhwtc(const void* y, void* x, int x_fmt, int64_t T, int64_t B, int64_t C, int64_t H,
+                    int64_t W, void* stream) {
+  if (!x || !y) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (x_fmt != CF_FMT_F32 && x_fmt != CF_FMT_F16) return fail(CF_ERR_INVALID_ARG, "bad x_fmt");
+  if (T < 0 || B < 0 || C <= 0 || H <= 0 || W <= 0) return fail(CF_ERR_INVALID_ARG, "bad shape");
+  if (T * B == 0) return CF_OK;
+  if (T * B * H > 0x7FFFFFFF) return fail(CF_ERR_UNSUPPORTED, "T*B*H too large");
+  if (int rc = require_sm100()) return rc;
+  dim3 grid((unsigned)((W + TB - 1) / TB), (unsigned)((C + TB - 1) / TB), (unsigned)(T * B * H));
+  unpack_kernel<<<grid, dim3(TB, 8), 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(y), x, x_fmt, (int)T, (int)B, (int)C, (int)H, (int)W);
+  return check_launch("unpack launch");
+}
+
+int cf_v_layout(const float* src, float* dst, int64_t B, int64_t C, int64_t H, int64_t W,
+                int to_nhwc, void* stream) {
+  if (!src || !dst || src == dst) return fail(CF_ERR_INVALID_ARG, "src/dst NULL or aliased");
+  if (B < 0 || C <= 0 || H <= 0 || W <= 0) return fail(CF_ERR_INVALID_ARG, "bad shape");
+  if (B == 0) return CF_OK;
+  if (B > 65535) return fail(CF_ERR_UNSUPPORTED, "B too large");
+  if (int rc = require_sm100()) return rc;
+  const int64_t HW = H * W;
+  dim3 grid((unsigned)((HW + TB - 1) / TB), (unsigned)((C + TB - 1) / TB), (unsigned)B);
+  v_layout_kernel<<<grid, dim3(TB, 8), 0, static_cast<cudaStream_t>(stream)>>>(
+      src, dst, (int)C, (int)HW, to_nhwc);
+  return check_launch("v_layout launch");
+}
+
+int cf_pack_conv_weight(const float* w, void* wp, int64_t Cout, int64_t Cin, int64_t KH,
+                        int64_t KW, int64_t Cin_p, void* stream) {
+  if (!w || !wp) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (Cout <= 0 || Cin <= 0 || KH <= 0 || KW <= 0 || Cin_p < Cin || Cin_p % 16)
+    return fail(CF_ERR_INVALID_ARG, "bad weight shape (Cin_p >= Cin, Cin_p %% 16 == 0)");
+  if (int rc = require_sm100()) return rc;
+  const int64_t n = Cout * KH * KW * Cin_p;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  pack_weight_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      w, static_cast<__half*>(wp), (int)Cout, (int)Cin, (int)KH, (int)KW, (int)Cin_p);
+  return check_launch("pack_weight launch");
+}
+
+int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b, float* logits, int64_t T,
+                  int64_t B, int64_t H, int64_t W, int64_t C, int64_t K, void* stream) {
+  if (!x || !fc_w || !logits) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || C <= 0 || K <= 0)
+    return fail(CF_ERR_INVALID_ARG, "bad shape");
+  if (C * 4 > 48 * 1024) return fail(CF_ERR_UNSUPPORTED, "C too large for the head kernel");
+  if (int rc = require_sm100()) return rc;
+  avgpool_fc_kernel<<<(unsigned)(T * B), 256, (size_t)C * 4, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), fc_w, fc_b, logits, (int)T, (int)B, (int)(H * W), (int)C,
+      (int)K);
+  return check_launch("avgpool_fc launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,227 @@
+/*
+ * catfuse_b200.h — C ABI of the B200-native (sm_100a) multi-step SNN inference
+ * kernels.  Every entry point:
+ *   - takes raw device pointers, sizes and scalars (no framework types);
+ *   - is stream-ordered on the `stream` argument (a cudaStream_t, passed as
+ *     void* so this header needs no CUDA include; NULL = legacy default stream);
+ *   - never allocates device memory and never synchronises the host;
+ *   - returns CF_OK (0) or a negative CF_ERR_* code; the message of the last
+ *     failure on the calling thread is available through cf_get_last_error().
+ * The device is the current CUDA device of the calling thread.
+ *
+ * Tensor layouts used by the fused conv path ("pixel-major, time-inner"):
+ *   activations  [B][H][W][T][C]   fp16 (spike counts {0,1,2,...} are exact)
+ *   membrane v   [B][H][W][C]      fp32
+ *   conv weights [Cout][KH][KW][Cin_p] fp16, Cin_p = Cin rounded up to 16
+ * The LIF-family kernels use the reference's own layout [T][B][C][H][W]
+ * (flattened as [T][N] with N = B*C*H*W).
+ *
+ * LIF semantics (SpikingJelly LIFNode, multi-step, as reproduced by CATFuse):
+ *   decay_input: h = v + (z - (v - v_reset)) / tau
+ *   otherwise  : h = v - (v - v_reset) / tau + z
+ *   spike s = (h >= v_threshold)
+ *   hard reset : v = s ? v_reset : h        soft reset: v = h - s * v_threshold
+ */
+#ifndef CATFUSE_B200_H
+#define CATFUSE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CF_API __attribute__((visibility("default")))
+#else
+#define CF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define CF_OK               0
+#define CF_ERR_INVALID_ARG (-1)   /* null pointer, bad size, bad enum      */
+#define CF_ERR_UNSUPPORTED (-2)   /* shape/alignment this build can't run  */
+#define CF_ERR_CUDA        (-3)   /* a CUDA runtime/driver call failed     */
+#define CF_ERR_NO_DEVICE   (-4)   /* no sm_100 device is current           */
+#define CF_ERR_DEVICE_TIMEOUT (-5)/* a bounded device-side wait expired    */
+
+/* ---- element formats ---------------------------------------------------- */
+#define CF_FMT_F32  0   /* float32                                       */
+#define CF_FMT_F16  1   /* float16                                       */
+#define CF_FMT_U8   2   /* uint8 (spikes / spike counts)                  */
+#define CF_FMT_BITS 3   /* bit-packed spikes: bit (i%32) of word i/32     */
+
+/* ---- residual modes of the fused conv epilogue -------------------------- */
+#define CF_RES_NONE      0  /* out = s                                      */
+#define CF_RES_ADD_POST  1  /* SEW 'ADD' : out = identity + s               */
+#define CF_RES_AND_POST  2  /* SEW 'AND' : out = identity * s               */
+#define CF_RES_IAND_POST 3  /* SEW 'IAND': out = identity * (1 - s)         */
+#define CF_RES_ADD_PRE   4  /* Spiking-ResNet: z += identity before the LIF */
+
+/* ---- library / error ---------------------------------------------------- */
+CF_API const char* cf_version(void);
+/* Copies the last error message of this thread into buf (always
+ * NUL-terminated) and returns its full length. */
+CF_API size_t cf_get_last_error(char* buf, size_t buf_len);
+/* 1 if the current device is sm_100 (B200-class), 0 otherwise. */
+CF_API int cf_device_supported(void);
+/* Reads and clears the device-side error word that bounded waits inside the
+ * kernels set on expiry (synchronises `stream`). Returns CF_OK, or
+ * CF_ERR_DEVICE_TIMEOUT with *code = the recorded site. */
+CF_API int cf_check_device_error(void* stream, int32_t* code);
+
+/* ---- bandwidth-bound LIF family (reference layout [T][N]) --------------- */
+
+/* Multi-step LIF over z[T][N].  Replaces `lif_sequential`
+ * (catfuse/sparseflow/lif_seq_kernel.py:51-90) and `lif_fwd_kernel`
+ * (catfuse/kernels/lif_fwd.py:39-72).  z_fmt: CF_FMT_F32 or CF_FMT_F16.
+ * v0 may be NULL (v0 = 0).  vT may be NULL (final v not stored).
+ * spike_fmt: F32 / F16 / U8 / BITS (BITS requires N % 32 == 0). */
+CF_API int cf_lif_fwd(const void* z, int z_fmt, const float* v0,
+               void* spikes, int spike_fmt, float* vT,
+               int64_t T, int64_t N,
+               float tau, float v_threshold, float v_reset,
+               int hard_reset, int decay_input, void* stream);
+
+/* Per-channel affine + LIF over z[T][B][C][HW]:  z' = z*scale[c] + shift[c]
+ * (+ identity when identity != NULL).  z == NULL means z == 0 (StaticZero:
+ * z' = shift).  Replaces `_bn_lif_state_carry_kernel`
+ * (catfuse/kernels/partial_fusion_conv_bn_lif_impl.py:110-154),
+ * `_bn_add_lif_state_carry_kernel`
+ * (catfuse/kernels/partial_fusion_conv_bn_add_lif_impl.py:76-123) and
+ * `static_zero_forward` (catfuse/implementations/base.py:250-308).
+ * scale may be NULL (=1).  identity_fmt: F32 or F16. */
+CF_API int cf_bn_lif(const void* z, int z_fmt, const float* scale, const float* shift,
+              const void* identity, int identity_fmt,
+              const float* v0, void* spikes, int spike_fmt, float* vT,
+              int64_t T, int64_t B, int64_t C, int64_t HW,
+              float tau, float v_threshold, float v_reset,
+              int hard_reset, int decay_input, void* stream);
+
+/* z = x1 + x2, then LIF.  Replaces `add_lif_block_kernel`
+ * (catfuse/kernels/add_lif.py:63-110). x1/x2 fp32 [T][N]. */
+CF_API int cf_add_lif(const float* x1, const float* x2, const float* v0,
+               void* spikes, int spike_fmt, float* vT, int64_t T, int64_t N,
+               float tau, float v_threshold, float v_reset,
+               int hard_reset, int decay_input, void* stream);
+
+/* k x k / stride k average pool over x[T][B][C][H][W] (fp32), then LIF on the
+ * pooled map [T][B][C][H/k][W/k].  Replaces `avgpool_lif_block_kernel`
+ * (catfuse/kernels/avgpool_lif.py:61-145).  H and W must be multiples of k. */
+CF_API int cf_avgpool_lif(const float* x, const float* v0, void* spikes, int spike_fmt,
+                   float* vT, int64_t T, int64_t B, int64_t C, int64_t H,
+                   int64_t W, int k, float tau, float v_threshold,
+                   float v_reset, int hard_reset, int decay_input,
+                   void* stream);
+
+/* ---- layout conversion ---------------------------------------------------- */
+
+/* x[T][B][C][H][W] (fp32 or fp16) -> y[B][H][W][T][Cp] fp16, channels
+ * C..Cp-1 zero-filled.  Cp >= C, Cp % 16 == 0. */
+CF_API int cf_pack_tbchw(const void* x, int x_fmt, void* y, int64_t T, int64_t B,
+                  int64_t C, int64_t H, int64_t W, int64_t Cp, void* stream);
+/* y[B][H][W][T][C] fp16 -> x[T][B][C][H][W] (fp32 or fp16). */
+CF_API int cf_unpack_bhwtc(const void* y, void* x, int x_fmt, int64_t T, int64_t B,
+                    int64_t C, int64_t H, int64_t W, void* stream);
+/* v[B][C][H][W] <-> v[B][H][W][C], fp32.  to_nhwc = 1: NCHW -> NHWC. */
+CF_API int cf_v_layout(const float* src, float* dst, int64_t B, int64_t C,
+                int64_t H, int64_t W, int to_nhwc, void* stream);
+/* w[Cout][Cin][KH][KW] fp32 -> wp[Cout][KH][KW][Cin_p] fp16 (zero-padded).
+ * Replaces SparseFlow's `_ensure_w_cl`
+ * (catfuse/implementations/sparse_flow.py:92-99). */
+CF_API int cf_pack_conv_weight(const float* w, void* wp, int64_t Cout, int64_t Cin,
+                        int64_t KH, int64_t KW, int64_t Cin_p, void* stream);
+
+/* ---- fused Conv -> BN -> LIF on tcgen05 ----------------------------------- */
+
+/* Tile geometry of cf_conv_bn_lif for a shape; lets the caller size the
+ * per-tile mask buffer.  out[0..5] = {Tp, Wb, Hb, Bb, n_mtiles, BN}. */
+CF_API int cf_conv_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo,
+                     int64_t Cout, int32_t* out6);
+
+/* Implicit-GEMM convolution on the 5th-generation tensor cores (fp16
+ * operands, fp32 accumulation in TMEM) with the BN affine, the optional
+ * residual and the multi-step LIF in the epilogue, looping over all time
+ * steps inside the kernel (z and v never reach HBM).
+ *   x        [B][H][W][T][Cin_p] fp16
+ *   wp       [Cout][KH][KW][Cin_p] fp16 (cf_pack_conv_weight)
+ *   scale/shift [Cout] fp32: z' = acc*scale + shift (scale NULL = 1)
+ *   identity [B][Ho][Wo][T][Cout] fp16 or NULL (see CF_RES_*)
+ *   v_in / v_out [B][Ho][Wo][Cout] fp32, either may be NULL (v_in NULL: v0=0);
+ *            v_in == v_out is allowed (in-place StateCarry)
+ *   out      [B][Ho][Wo][T][Cout] fp16
+ *   tile_mask per-M-tile bit mask of active input channel chunks
+ *            (cf_prescan_conv_tiles) or NULL (dense: DenseKeep).  A tile whose
+ *            mask is 0 runs no MMA at all (StaticZero for that tile).
+ * Replaces DenseKeep.forward (catfuse/implementations/dense_keep.py:97-155),
+ * SparseFlow.forward + `sparse_streamfuse_conv3x3_bn_lif`
+ * (catfuse/implementations/sparse_flow.py:186-270,
+ *  catfuse/sparseflow/streamfuse_kernel.py:32-187) and the per-step
+ * `fused_bm_conv3x3_bn_lif_8x8/8x16`
+ * (catfuse/sparseflow/fused_conv_bn_lif_kernel.py:63-335).
+ * Requirements: Cin_p % 16 == 0, Cout % 32 == 0, 1 <= T. */
+CF_API int cf_conv_bn_lif(const void* x, const void* wp, const float* scale,
+                   const float* shift, const void* identity, int res_mode,
+                   const float* v_in, float* v_out, void* out,
+                   const uint32_t* tile_mask,
+                   int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin_p,
+                   int64_t Cout, int64_t KH, int64_t KW, int64_t stride,
+                   int64_t pad, float tau, float v_threshold, float v_reset,
+                   int hard_reset, int decay_input, void* stream);
+
+/* Linear -> (BN1d) -> LIF over tokens: x [B][L][T][Cin_p] fp16,
+ * w [Cout][Cin_p] fp16, out [B][L][T][Cout] fp16.  A 1x1 convolution on the
+ * same tensor-core kernel.  Replaces FusedLinearLIF
+ * (catfuse/patterns.py:493-596) and `linear_lif_block_kernel`
+ * (catfuse/kernels/linear_lif.py:51-102). */
+CF_API int cf_linear_bn_lif(const void* x, const void* w, const float* scale,
+                     const float* shift, const void* identity, int res_mode,
+                     const float* v_in, float* v_out, void* out,
+                     int64_t T, int64_t B, int64_t L, int64_t Cin_p,
+                     int64_t Cout, float tau, float v_threshold,
+                     float v_reset, int hard_reset, int decay_input,
+                     void* stream);
+
+/* ---- SparseFlow prescan ---------------------------------------------------- */
+
+/* Receptive-field prescan with the reference's geometry over x[N][C][H][W]
+ * (N = T*B): bit g of ag_mask[n][gh][gw] is 1 iff some |x| > threshold in
+ * channels [g*GS, (g+1)*GS) of the receptive field of the tile's valid output
+ * pixels; tile_class = 0 (mask 0), 2 (all groups), else 1; nnz_out (int64,
+ * may be NULL) receives the number of nonzero elements of x (atomically
+ * accumulated: the caller zeroes it).  Replaces
+ * `fast_spike_prescan_2d_v2` (catfuse/sparseflow/fast_prescan_v2.py:92-137)
+ * and `build_rf_prescan_metadata` (catfuse/sparseflow/prescan.py:153-189).
+ * x_fmt: F32 / F16 / U8.  NUM_GROUPS = ceil(C/GS) must be <= 32. */
+CF_API int cf_prescan(const void* x, int x_fmt, int32_t* ag_mask, int32_t* tile_class,
+               int64_t* nnz_out, int64_t N, int64_t C, int64_t H, int64_t W,
+               int64_t H_out, int64_t W_out, int64_t k, int64_t stride,
+               int64_t pad, int64_t BH, int64_t BW, int64_t GS,
+               float threshold, void* stream);
+
+/* Prescan in the fused conv kernel's own tile geometry over
+ * x[B][H][W][T][Cin_p] fp16: mask[m] bit c = 1 iff a nonzero exists in input
+ * channel chunk c (chunk = `chunk` channels) of M-tile m's receptive field,
+ * over the tile's time steps.  nnz_out as for cf_prescan (may be NULL). */
+CF_API int cf_prescan_conv_tiles(const void* x, uint32_t* mask, int64_t* nnz_out,
+                          int64_t T, int64_t B, int64_t H, int64_t W,
+                          int64_t Cin_p, int64_t Cout, int64_t KH, int64_t KW,
+                          int64_t stride, int64_t pad, int64_t chunk,
+                          void* stream);
+/* Channel chunk the conv kernel uses for a given Cin_p in sparse mode. */
+CF_API int cf_conv_chunk(int64_t Cin_p, int sparse);
+
+/* ---- network head ---------------------------------------------------------- */
+
+/* Global average pool over x[B][H][W][T][C] fp16 then fc: logits[T][B][K] =
+ * mean_hw(x) @ fc_w[K][C]^T + fc_b (fc_b may be NULL).  The SEW/Spiking
+ * ResNet classifier (avgpool -> flatten(2) -> fc). */
+CF_API int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b,
+                  float* logits, int64_t T, int64_t B, int64_t H, int64_t W,
+                  int64_t C, int64_t K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CATFUSE_B200_H */
