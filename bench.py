@@ -1,0 +1,356 @@
+"""Benchmark: SEW-ResNet-18 (CIFAR shape, T=4) inference samples/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = ``functional.reset_net`` + one multi-step forward of SEW-ResNet-18
+(B=64 per GPU, 3x32x32 N(0,1) images repeated over T=4,
+random-init weights with data-calibrated BN statistics, LIF tau=2, v_th=1,
+hard reset, cnf ADD, avgpool -> fc 512->10).  With N GPUs (torchrun, one
+process per GPU) every rank runs its own batch of 64 (weak scaling) and the
+logits are all-gathered over NCCL at the end of each step.
+
+``value``: samples/s of the whole job with inputs resident in HBM (the
+forward is one CUDA-graph replay of fused sm_100a kernels), each step timed
+with CUDA events, L2 flushed (256 MB write) between steps outside the timed
+events, max over ranks.  ``e2e``: the same metric through the public API
+(``optimize``'d model called on a device copy of pinned host images, logits
+read back to the host), host<->device copies inside the timed region.
+``--impl reference``: the reference's CPU path (SpikingJelly semantics in
+PyTorch, restated in ``oracle/``) on the host cores; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SEW-ResNet18 T=4 samples/s"
+UNIT = "samples/s"
+T_STEPS = 4
+BATCH = 64
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _conv_flops(plan) -> float:
+    from catfuse_b200.network import ConvStep
+    total = 0.0
+    for st in plan.steps:
+        if isinstance(st, ConvStep):
+            b, ho, wo, t, co = plan.shapes[st.dst]
+            spec = st.native.spec
+            total += 2.0 * t * b * ho * wo * co * spec.in_channels * spec.kernel_size ** 2
+    return total
+
+
+def _traffic_from_profiles():
+    """Per-launch DRAM bytes of the conv kernel from the committed ncu summary
+    (a line 'traffic_bytes_per_forward: N'), or None."""
+    p = ROOT / "profiles" / "conv_bn_lif_sew_rn18.md"
+    try:
+        for line in p.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch_avg:"):
+                return float(line.split(":", 1)[1])
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_model(device, batch, seed=0):
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import zoo
+    net = zoo.init_random_(zoo.build_sew_resnet18_cifar(), seed)
+    g = torch.Generator().manual_seed(1000 + seed)
+    calib = torch.randn(batch, 3, 32, 32, generator=g).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+    zoo.calibrate_bn_(net, calib)
+    model, stats = optimize(net.eval(), device=device, T=T_STEPS)
+    return model, stats, net
+
+
+def cpu_baseline(batch=16, budget_s=12.0):
+    """The reference's CPU path (SJ semantics in PyTorch; oracle restatement)
+    on the host cores, a bounded sample of the workload."""
+    import oracle
+    from catfuse_b200.sj import zoo
+    torch.set_num_threads(os.cpu_count() or 1)
+    net = zoo.init_random_(zoo.build_sew_resnet18_cifar(), 0)
+    g = torch.Generator().manual_seed(1000)
+    x = torch.randn(batch, 3, 32, 32, generator=g).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+    zoo.calibrate_bn_(net, x)
+    params = {k: v.detach().float() for k, v in net.state_dict().items()}
+    with torch.no_grad():
+        oracle.sew_resnet18_forward(x, params)  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            oracle.sew_resnet18_forward(x, params)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or n >= 50:
+                break
+    return {"value": n * batch / el, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} forwards of B={batch} (T=4, 32x32) in {el:.1f}s, fp32 torch CPU "
+                      f"(SpikingJelly LIF semantics, oracle/nets.py)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    budget = max(2.0, min(20.0, 60.0 / max(args.steps + args.warmup, 1)))
+    for _ in range(args.warmup):
+        cpu_baseline(batch=8, budget_s=0.5)
+    vals = [cpu_baseline(batch=16, budget_s=budget) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in vals)
+    base = vals[0]
+    base["value"] = v
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * 16 / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "SEW-ResNet18 CIFAR T=4 forward (reference CPU path)",
+                       "global_batch": 16, "seq_len": T_STEPS, "parallelism": "cpu"},
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    from catfuse_b200.sj import functional
+    model, stats, _ = build_model(dev, args.batch)
+    B = args.batch
+    g = torch.Generator().manual_seed(2000 + rank)
+    images = torch.randn(B, 3, 32, 32, generator=g)
+    x_dev = images.to(dev).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1).contiguous()
+    plan = model.plan_for(x_dev)
+    plan.x_in.copy_(x_dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    gathered = torch.empty((world, T_STEPS, B, 10), device=dev) if world > 1 else None
+
+    def step():
+        plan.fresh = True            # reset_net: every step starts from v = 0
+        logits = plan.run(use_graph=True)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, logits)
+        return logits
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- value: device-resident inputs, per-step CUDA events, L2 flushed ----
+    sampler = ClockSampler(local)
+    sampler.start()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for s, e in evs:
+        flush.fill_(1.0)
+        s.record()
+        step()
+        e.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in evs]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = world * B * args.steps / (total_ms / 1000.0)
+
+    # ---- kernel roofline: each conv launch timed alone with events ----------
+    from catfuse_b200.network import ConvStep
+    from catfuse_b200 import ops
+    conv_ms = []
+    for _ in range(3):
+        plan.fresh = True
+        ev = []
+        ops.pack_tbchw(plan.x_in, plan.shapes[0][-1], out=plan.acts[0])
+        for st in plan.steps:
+            if not isinstance(st, ConvStep):
+                continue
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            spec = st.native.spec
+            ident = plan.acts[st.identity] if st.identity is not None else None
+            flush.fill_(1.0)
+            a.record()
+            mode = "z_only" if st.lif is None else (st.res_mode if ident is not None else "none")
+            ops.conv_bn_lif(plan.acts[st.src], st.wp, st.scale, st.shift, spec.stride, spec.padding,
+                            identity=ident if st.lif is not None else None, res_mode=mode,
+                            v_in=None, v_out=st.v, lif=st.lif or ops.LIFConfig(),
+                            out=plan.acts[st.dst])
+            b.record()
+            ev.append((a, b))
+        torch.cuda.synchronize()
+        conv_ms.append(sum(a.elapsed_time(b) for a, b in ev))
+    n_conv = sum(1 for st in plan.steps if isinstance(st, ConvStep))
+    conv_ms_fwd = min(conv_ms)
+    flops = _conv_flops(plan)
+    peaks, peak_src = _peaks()
+    achieved = flops / (conv_ms_fwd / 1000.0) / 1e12
+    traffic = _traffic_from_profiles()
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "traffic": traffic, "peak_source": f"{peak_src} bf16_tflops (burst)",
+                "kernel": "conv_bn_lif_kernel (all 20 conv launches of one forward)",
+                "flops_per_forward": flops, "conv_ms_per_forward": conv_ms_fwd,
+                "launches_per_forward": n_conv,
+                "share_of_step": conv_ms_fwd / ms_per_step}
+
+    # ---- e2e through the public API (host buffers, copies inside) -----------
+    pinned = images.pin_memory()
+    out_host = torch.empty((T_STEPS, B, 10), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        xd = pinned.to(dev, non_blocking=True)
+        x_seq = xd.unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+        functional.reset_net(model)
+        logits = model(x_seq)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, logits)
+        out_host.copy_(logits, non_blocking=True)
+        return logits
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    t = torch.tensor([e2e_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * args.steps / (float(t.item()) / 1000.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "SEW-ResNet18 CIFAR T=4 forward (BASELINE config 1)",
+                       "model": "sew_resnet18_cifar", "global_batch": world * B,
+                       "per_gpu_batch": B, "seq_len": T_STEPS, "parallelism": f"dp{world}",
+                       "l2": "flushed (256 MB write) between timed steps",
+                       "weights": "random init (seed 0), BN statistics calibrated on synthetic data",
+                       "operands": "fp16 spikes/weights, fp32 accumulate + LIF"},
+            "gpu_launches": plan.launches() * args.steps,
+            "roofline": roofline,
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": pinned.numel() * 4,
+                    "d2h_bytes_per_step": out_host.numel() * 4},
+            "clocks": clocks,
+            "routing": {k: v for k, v in stats["patterns_matched"].items()},
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -21,7 +21,7 @@ CF_ERR_NO_DEVICE = -4
 CF_ERR_DEVICE_TIMEOUT = -5
 
 FMT_F32, FMT_F16, FMT_U8, FMT_BITS = 0, 1, 2, 3
-RES_NONE, RES_ADD_POST, RES_AND_POST, RES_IAND_POST, RES_ADD_PRE = 0, 1, 2, 3, 4
+RES_NONE, RES_ADD_POST, RES_AND_POST, RES_IAND_POST, RES_ADD_PRE, RES_Z_ONLY = 0, 1, 2, 3, 4, 5
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -55,6 +55,7 @@ SIGNATURES = {
     "cf_prescan_conv_tiles": (_INT, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                      _I64, _I64, _I64, _P]),
     "cf_conv_chunk": (_INT, [_I64, _INT]),
+    "cf_maxpool_bhwtc": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "cf_avgpool_fc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
 }
 

@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
             const int64_t row = (pix * a.T + a.t0 + t) * a.Cout + col0;
             float idv[CW];
-            if (a.res_mode != CF_RES_NONE && pix_ok) {
+            if (a.res_mode != CF_RES_NONE && a.res_mode != CF_RES_Z_ONLY && pix_ok) {
               const __half2* ip = reinterpret_cast<const __half2*>(a.identity + row);
 #pragma unroll
               for (int j = 0; j < CW / 2; ++j) {
@@ -349,6 +349,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               if (a.res_mode == CF_RES_ADD_PRE) {
                 zz0 = __fadd_rn(zz0, idv[j]);
                 zz1 = __fadd_rn(zz1, idv[j + 1]);
+              }
+              if (a.res_mode == CF_RES_Z_ONLY) {
+                o[j / 2] = __floats2half2_rn(zz0, zz1);
+                continue;
               }
               float s0 = lif_step(v[j], zz0, a.lp);
               float s1 = lif_step(v[j + 1], zz1, a.lp);
@@ -374,7 +378,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
           }
         }
-        if (a.v_out && pix_ok) {
+        if (a.v_out && pix_ok && a.res_mode != CF_RES_Z_ONLY) {
           float4* vp = reinterpret_cast<float4*>(a.v_out + pix * a.Cout + col0);
 #pragma unroll
           for (int j = 0; j < CW / 4; ++j)
@@ -574,12 +578,12 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   if (Cin_p % 16) return fail(CF_ERR_UNSUPPORTED, "Cin_p must be a multiple of 16");
   if (Cout % 32) return fail(CF_ERR_UNSUPPORTED, "Cout must be a multiple of 32");
   if (stride > 8) return fail(CF_ERR_UNSUPPORTED, "stride must be <= 8");
-  if (res_mode < CF_RES_NONE || res_mode > CF_RES_ADD_PRE)
+  if (res_mode < CF_RES_NONE || res_mode > CF_RES_Z_ONLY)
     return fail(CF_ERR_INVALID_ARG, "bad residual mode %d", res_mode);
-  if (res_mode != CF_RES_NONE && !identity)
+  if (res_mode != CF_RES_NONE && res_mode != CF_RES_Z_ONLY && !identity)
     return fail(CF_ERR_INVALID_ARG, "residual mode needs an identity tensor");
   if (!(tau > 0.f)) return fail(CF_ERR_INVALID_ARG, "tau must be > 0");
-  if (T > kMaxTP && !v_out)
+  if (T > kMaxTP && !v_out && res_mode != CF_RES_Z_ONLY)
     return fail(CF_ERR_INVALID_ARG,
                 "T > %d runs in time blocks and needs v_out to carry the membrane", kMaxTP);
   const void* ptrs16[] = {x, wp, identity, v_in, v_out, out};

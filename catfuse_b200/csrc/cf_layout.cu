@@ -137,6 +137,40 @@ __global__ void avgpool_fc_kernel(const __half* __restrict__ x, const float* __r
   }
 }
 
+// Max pool over x[B][H][W][T][C] fp16 (padding = -inf), one thread per
+// output element group of 8 channels (16-byte vectors).
+__global__ void maxpool_kernel(const __half* __restrict__ x, __half* __restrict__ y, int B, int H,
+                               int W, int T, int C, int Ho, int Wo, int k, int s, int p) {
+  const int cv = C / 8;
+  const int64_t n = (int64_t)B * Ho * Wo * T * cv;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int c8 = (int)(i % cv);
+    int64_t r = i / cv;
+    const int t = (int)(r % T); r /= T;
+    const int wo = (int)(r % Wo); r /= Wo;
+    const int ho = (int)(r % Ho);
+    const int b = (int)(r / Ho);
+    __half2 m[4];
+    const __half2 neg = __float2half2_rn(-65504.f);
+    for (int j = 0; j < 4; ++j) m[j] = neg;
+    for (int dh = 0; dh < k; ++dh) {
+      const int ih = ho * s - p + dh;
+      if (ih < 0 || ih >= H) continue;
+      for (int dw = 0; dw < k; ++dw) {
+        const int iw = wo * s - p + dw;
+        if (iw < 0 || iw >= W) continue;
+        const uint4 u = *reinterpret_cast<const uint4*>(
+            x + ((((int64_t)b * H + ih) * W + iw) * T + t) * C + c8 * 8);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+        for (int j = 0; j < 4; ++j) m[j] = __hmax2(m[j], h[j]);
+      }
+    }
+    *reinterpret_cast<uint4*>(y + ((((int64_t)b * Ho + ho) * Wo + wo) * T + t) * C + c8 * 8) =
+        *reinterpret_cast<const uint4*>(m);
+  }
+}
+
 }  // namespace
 }  // namespace cf
 
@@ -212,6 +246,26 @@ int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b, float* lo
       static_cast<const __half*>(x), fc_w, fc_b, logits, (int)T, (int)B, (int)(H * W), (int)C,
       (int)K);
   return check_launch("avgpool_fc launch");
+}
+
+int cf_maxpool_bhwtc(const void* x, void* y, int64_t B, int64_t H, int64_t W, int64_t T,
+                     int64_t C, int64_t k, int64_t stride, int64_t pad, void* stream) {
+  if (!x || !y) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (B <= 0 || H <= 0 || W <= 0 || T <= 0 || C <= 0 || k <= 0 || stride <= 0 || pad < 0 ||
+      pad > k / 2)
+    return fail(CF_ERR_INVALID_ARG, "bad maxpool shape");
+  if (C % 8) return fail(CF_ERR_UNSUPPORTED, "C must be a multiple of 8");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) != 0)
+    return fail(CF_ERR_UNSUPPORTED, "x and y must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  const int64_t Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
+  const int64_t n = B * Ho * Wo * T * (C / 8);
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  maxpool_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), static_cast<__half*>(y), (int)B, (int)H, (int)W, (int)T,
+      (int)C, (int)Ho, (int)Wo, (int)k, (int)stride, (int)pad);
+  return check_launch("maxpool launch");
 }
 
 }  // extern "C"

@@ -1,0 +1,297 @@
+"""Native network executor for rewritten spiking ResNets.
+
+After the rewrite, a SEW / Spiking ResNet is a chain of fused conv patterns.
+Running them one by one through their module ``forward`` would convert
+layouts at every boundary; :class:`CTFNetwork` instead compiles the chain into
+a :class:`NetworkPlan` — one pack kernel, one fused Conv->BN->LIF launch per
+conv layer (the SEW residual combine fused into the epilogue of the block's
+second conv), an optional max-pool, and the avgpool+fc head — over static
+buffers in the kernels' [B, H, W, T, C] fp16 layout, captured into a CUDA
+graph per input shape.  The rewritten module tree stays attached (state
+dicts, routing stats, module-level use).
+
+Membrane state: every LIF layer owns a v buffer [B, H, W, C] fp32 in the plan.
+After ``reset()`` (``functional.reset_net``) the next forward starts from
+v = 0 (the kernels skip the read); otherwise v_T of the previous forward is
+carried in (StateCarry), as SpikingJelly does.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .ops import LIFConfig
+from .patterns import (CTFSEWBasicBlock, CTFSpikingBasicBlock, PartialFusionConvBNLIF,
+                       STFusionConvBNLIF, _ConvBN)
+from .sj.neuron import is_lif
+
+
+class UnsupportedTopology(ValueError):
+    pass
+
+
+@dataclass
+class ConvStep:
+    name: str
+    native: object                # patterns.NativeConv
+    src: int                      # activation buffer index
+    dst: int
+    identity: Optional[int] = None
+    res_mode: str = "none"
+    lif: Optional[LIFConfig] = None   # None: z-only (Conv+BN branch)
+    sparse: bool = False
+    # filled at build time
+    v: Optional[torch.Tensor] = None
+    mask: Optional[torch.Tensor] = None
+    wp: Optional[torch.Tensor] = None
+    scale: Optional[torch.Tensor] = None
+    shift: Optional[torch.Tensor] = None
+
+
+@dataclass
+class PoolStep:
+    src: int
+    dst: int
+    k: int
+    s: int
+    p: int
+
+
+@dataclass
+class Graphable:
+    steps: List[object] = field(default_factory=list)
+
+
+def _native_of(m):
+    if hasattr(m, "native_conv"):
+        return m.native_conv()
+    raise UnsupportedTopology(f"{type(m).__name__} is not a fused conv pattern")
+
+
+def _lif_of(m) -> LIFConfig:
+    return LIFConfig(float(m.tau), float(m.v_threshold),
+                     None if m.v_reset is None else float(m.v_reset),
+                     bool(getattr(m, "decay_input", True)))
+
+
+def _stem_pattern(model):
+    c = model.conv1
+    if isinstance(c, (PartialFusionConvBNLIF, STFusionConvBNLIF)):
+        return c
+    if isinstance(c, nn.Conv2d) and isinstance(model.bn1, nn.BatchNorm2d) and is_lif(model.sn1):
+        return PartialFusionConvBNLIF.from_sj_modules(c, model.bn1, model.sn1).to(c.weight.device)
+    raise UnsupportedTopology("stem is not Conv-BN-LIF")
+
+
+def _block_parts(b):
+    """-> (kind, first, second, downsample, cnf) with fused patterns."""
+    if isinstance(b, CTFSEWBasicBlock):
+        return "sew", b.fused_first, b.fused_second, b.fused_downsample, b.cnf
+    if isinstance(b, CTFSpikingBasicBlock):
+        return "spiking", b.fused_first, b.fused_second_add, b.downsample, None
+    if type(b).__name__ == "BasicBlock":
+        first, second = b.conv1, b.conv2
+        if not hasattr(first, "native_conv") or not hasattr(second, "native_conv"):
+            raise UnsupportedTopology("block convs are not fused")
+        ds = None
+        if getattr(b, "downsample", None) is not None:
+            ds = b.downsample[0] if isinstance(b.downsample, nn.Sequential) else b.downsample
+            if not hasattr(ds, "native_conv"):
+                raise UnsupportedTopology("downsample is not fused")
+        if getattr(b, "cnf", None) is None:
+            raise UnsupportedTopology("un-rewritten standard Spiking BasicBlock")
+        return "sew", first, second, ds, b.cnf
+    raise UnsupportedTopology(f"unsupported block {type(b).__name__}")
+
+
+class NetworkPlan:
+    """Kernel launch list + static buffers for one input shape."""
+
+    def __init__(self, model: nn.Module, T: int, B: int, H: int, W: int, device,
+                 use_sparse: bool = False):
+        self.T, self.B, self.H, self.W = T, B, H, W
+        self.device = torch.device(device)
+        self.steps = []
+        self.shapes = []  # activation buffer shapes (B, H, W, T, C)
+        stem = _stem_pattern(model)
+        cin = stem.in_channels
+        self.in_channels = cin
+        self.x_in = torch.zeros((T, B, cin, H, W), dtype=torch.float32, device=self.device)
+        self.shapes.append((B, H, W, T, ops.pad16(cin)))
+        cur = 0
+
+        def add_conv(name, pat, src, identity=None, res_mode="none", lif=True):
+            nat = _native_of(pat)
+            spec = nat.spec
+            b_, h_, w_, t_, c_ = self.shapes[src]
+            ho, wo = spec.output_hw(h_, w_)
+            self.shapes.append((b_, ho, wo, t_, spec.out_channels))
+            dst = len(self.shapes) - 1
+            sparse = use_sparse and isinstance(pat, STFusionConvBNLIF)
+            self.steps.append(ConvStep(name, nat, src, dst, identity, res_mode,
+                                       _lif_of(pat) if lif else None, sparse))
+            return dst
+
+        cur = add_conv("stem", stem, cur)
+        mp = getattr(model, "maxpool", None)
+        if isinstance(mp, nn.MaxPool2d):
+            k = mp.kernel_size if isinstance(mp.kernel_size, int) else mp.kernel_size[0]
+            s = mp.stride if isinstance(mp.stride, int) else mp.stride[0]
+            p = mp.padding if isinstance(mp.padding, int) else mp.padding[0]
+            b_, h_, w_, t_, c_ = self.shapes[cur]
+            self.shapes.append((b_, (h_ + 2 * p - k) // s + 1, (w_ + 2 * p - k) // s + 1, t_, c_))
+            self.steps.append(PoolStep(cur, len(self.shapes) - 1, k, s, p))
+            cur = len(self.shapes) - 1
+        elif mp is not None and not isinstance(mp, nn.Identity):
+            raise UnsupportedTopology(f"unsupported pooling {type(mp).__name__}")
+
+        for li in range(1, 5):
+            stage = getattr(model, f"layer{li}")
+            for bi, blk in enumerate(stage):
+                kind, first, second, ds, cnf = _block_parts(blk)
+                nm = f"layer{li}.{bi}"
+                x_in = cur
+                h1 = add_conv(nm + ".conv1", first, x_in)
+                if kind == "sew":
+                    ident = add_conv(nm + ".downsample", ds, x_in) if ds is not None else x_in
+                    cur = add_conv(nm + ".conv2", second, h1, ident, cnf)
+                else:
+                    ident = x_in
+                    if ds is not None:
+                        ident = add_conv(nm + ".downsample", ds, x_in, lif=False)
+                    cur = add_conv(nm + ".conv2", second, h1, ident, "add_pre")
+        self.final = cur
+        fc = model.fc
+        if not isinstance(fc, nn.Linear):
+            raise UnsupportedTopology("classifier is not Linear")
+        self.fc_w = fc.weight.detach().float().contiguous().to(self.device)
+        self.fc_b = None if fc.bias is None else fc.bias.detach().float().contiguous().to(self.device)
+        self.logits = torch.zeros((T, B, fc.out_features), dtype=torch.float32, device=self.device)
+        self.acts = [torch.zeros(s, dtype=torch.float16, device=self.device) for s in self.shapes]
+        for st in self.steps:
+            if isinstance(st, ConvStep):
+                st.wp, st.scale, st.shift = st.native.packed(self.device)
+                b_, ho, wo, t_, co = self.shapes[st.dst]
+                if st.lif is not None:
+                    st.v = torch.zeros((b_, ho, wo, co), dtype=torch.float32, device=self.device)
+                if st.sparse:
+                    g = ops.conv_geometry(t_, b_, ho, wo, co)
+                    st.mask = torch.zeros(g["n_mtiles"], dtype=torch.int32, device=self.device)
+        self.fresh = True
+        self._graphs = {}
+
+    # ---- execution ---------------------------------------------------------
+    def launches(self) -> int:
+        n = 2  # pack + head
+        for st in self.steps:
+            n += 1 + (1 if isinstance(st, ConvStep) and st.sparse else 0)
+        return n
+
+    def run_eager(self, fresh: bool):
+        ops.pack_tbchw(self.x_in, self.shapes[0][-1], out=self.acts[0])
+        for st in self.steps:
+            if isinstance(st, PoolStep):
+                ops.maxpool_bhwtc(self.acts[st.src], st.k, st.s, st.p, out=self.acts[st.dst])
+                continue
+            b_, h_, w_, t_, c_ = self.shapes[st.src]
+            spec = st.native.spec
+            if st.sparse:
+                ops.prescan_conv_tiles(self.acts[st.src], spec.out_channels, spec.kernel_size,
+                                       spec.kernel_size, spec.stride, spec.padding,
+                                       mask_out=st.mask)
+            ident = self.acts[st.identity] if st.identity is not None else None
+            if st.lif is None:
+                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, spec.stride,
+                                spec.padding, res_mode="z_only", out=self.acts[st.dst])
+            else:
+                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, spec.stride,
+                                spec.padding, identity=ident,
+                                res_mode=st.res_mode if ident is not None else "none",
+                                v_in=None if fresh else st.v, v_out=st.v,
+                                tile_mask=st.mask if st.sparse else None, lif=st.lif,
+                                out=self.acts[st.dst])
+        ops.avgpool_fc(self.acts[self.final], self.fc_w, self.fc_b, out=self.logits)
+
+    def run(self, use_graph: bool = True):
+        fresh = self.fresh
+        if not use_graph:
+            self.run_eager(fresh)
+        else:
+            g = self._graphs.get(fresh)
+            if g is None:
+                # warm up on a side stream (the graph-capture protocol), then capture
+                s = torch.cuda.Stream(device=self.device)
+                s.wait_stream(torch.cuda.current_stream(self.device))
+                saved = [st.v.clone() for st in self.steps if isinstance(st, ConvStep) and st.v is not None]
+                with torch.cuda.stream(s):
+                    self.run_eager(fresh)
+                torch.cuda.current_stream(self.device).wait_stream(s)
+                i = 0
+                for st in self.steps:
+                    if isinstance(st, ConvStep) and st.v is not None:
+                        st.v.copy_(saved[i])
+                        i += 1
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self.run_eager(fresh)
+                self._graphs[fresh] = g
+            g.replay()
+        self.fresh = False
+        return self.logits
+
+    def layer_states(self):
+        """{layer name: v_T in the reference layout [B, C, H, W]}."""
+        out = {}
+        for st in self.steps:
+            if isinstance(st, ConvStep) and st.v is not None:
+                out[st.name] = ops.v_to_nchw(st.v)
+        return out
+
+
+class CTFNetwork(nn.Module):
+    """Wraps a rewritten spiking ResNet; ``forward(x[T, B, C, H, W])`` runs the
+    native plan and returns logits [T, B, classes] (fp32)."""
+
+    def __init__(self, model: nn.Module, use_graph: bool = True, use_sparse: bool = False):
+        super().__init__()
+        self.model = model
+        self.use_graph = use_graph
+        self.use_sparse = use_sparse
+        self._plans = {}
+        self._fresh = True
+        # validate now (raises UnsupportedTopology)
+        _stem_pattern(model)
+        for li in range(1, 5):
+            for blk in getattr(model, f"layer{li}"):
+                _block_parts(blk)
+
+    def reset(self):
+        self._fresh = True
+        for p in self._plans.values():
+            p.fresh = True
+
+    def plan_for(self, x: torch.Tensor) -> NetworkPlan:
+        T, B, C, H, W = x.shape
+        key = (T, B, C, H, W, x.device)
+        p = self._plans.get(key)
+        if p is None:
+            p = NetworkPlan(self.model, T, B, H, W, x.device, self.use_sparse)
+            self._plans[key] = p
+        return p
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dim() != 5:
+            raise ValueError("expected x[T, B, C, H, W]")
+        if not x.is_cuda:
+            raise RuntimeError("CTFNetwork runs on an sm_100 GPU only (CPU tensor given)")
+        p = self.plan_for(x)
+        if self._fresh:
+            p.fresh = True
+            self._fresh = False
+        p.x_in.copy_(x)
+        return p.run(self.use_graph).clone()

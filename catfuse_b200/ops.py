@@ -14,12 +14,12 @@ import torch
 
 from . import _lib
 from ._lib import (FMT_BITS, FMT_F16, FMT_F32, FMT_U8, RES_ADD_POST, RES_ADD_PRE,
-                   RES_AND_POST, RES_IAND_POST, RES_NONE, CatfuseNativeError)
+                   RES_AND_POST, RES_IAND_POST, RES_NONE, RES_Z_ONLY, CatfuseNativeError)
 
 __all__ = [
     "LIFConfig", "lif_fwd", "bn_lif", "add_lif", "avgpool_lif", "pack_tbchw", "unpack_bhwtc",
     "v_to_nhwc", "v_to_nchw", "pack_conv_weight", "conv_bn_lif", "linear_bn_lif",
-    "conv_geometry", "prescan", "prescan_conv_tiles", "conv_chunk", "avgpool_fc",
+    "conv_geometry", "prescan", "prescan_conv_tiles", "conv_chunk", "avgpool_fc", "maxpool_bhwtc",
     "pad16", "SPIKE_FORMATS", "RES_MODES",
 ]
 
@@ -27,7 +27,7 @@ SPIKE_FORMATS = {torch.float32: FMT_F32, torch.float16: FMT_F16, torch.uint8: FM
                  "bits": FMT_BITS}
 RES_MODES = {None: RES_NONE, "none": RES_NONE, "add": RES_ADD_POST, "ADD": RES_ADD_POST,
              "and": RES_AND_POST, "AND": RES_AND_POST, "iand": RES_IAND_POST,
-             "IAND": RES_IAND_POST, "add_pre": RES_ADD_PRE}
+             "IAND": RES_IAND_POST, "add_pre": RES_ADD_PRE, "z_only": RES_Z_ONLY}
 
 
 @dataclass(frozen=True)
@@ -361,6 +361,20 @@ def prescan_conv_tiles(x: torch.Tensor, Cout: int, KH: int, KW: int, stride: int
     _lib.call("cf_prescan_conv_tiles", x.data_ptr(), mask_out.data_ptr(), _ptr(nnz_out), T, B, H, W,
               Cin_p, Cout, KH, KW, stride, pad, chunk, _stream())
     return mask_out
+
+
+def maxpool_bhwtc(x: torch.Tensor, k: int, stride: int, pad: int,
+                  out: Optional[torch.Tensor] = None):
+    """Max pool over x[B,H,W,T,C] fp16 (k, stride, pad) -> [B,Ho,Wo,T,C]."""
+    _need(x, "x", torch.float16)
+    B, H, W, T, C = x.shape
+    Ho = (H + 2 * pad - k) // stride + 1
+    Wo = (W + 2 * pad - k) // stride + 1
+    if out is None:
+        out = torch.empty((B, Ho, Wo, T, C), dtype=torch.float16, device=x.device)
+    _lib.call("cf_maxpool_bhwtc", x.data_ptr(), out.data_ptr(), B, H, W, T, C, k, stride, pad,
+              _stream())
+    return out
 
 
 def avgpool_fc(x: torch.Tensor, fc_w: torch.Tensor, fc_b: Optional[torch.Tensor],

@@ -200,3 +200,52 @@ def load_params(net: nn.Module, params: dict) -> nn.Module:
     if missing or unexpected:
         raise KeyError(f"parameter mismatch: missing={missing[:5]} unexpected={unexpected[:5]}")
     return net
+
+
+@torch.no_grad()
+def init_random_(net: nn.Module, seed: int = 0) -> nn.Module:
+    """Seeded random init for benchmarking without a checkpoint: Kaiming-normal
+    conv weights (fan_in), BN eval statistics mean ~ N(0, 0.1),
+    var ~ U(0.5, 1.5), gamma ~ U(0.8, 1.2), beta ~ N(0, 0.1) (the BN setting of
+    the single-layer benchmark config), default Linear init."""
+    g = torch.Generator().manual_seed(seed)
+    for m in net.modules():
+        if isinstance(m, nn.Conv2d):
+            fan_in = m.in_channels * m.kernel_size[0] * m.kernel_size[1] // m.groups
+            m.weight.copy_(torch.randn(m.weight.shape, generator=g) * (2.0 / fan_in) ** 0.5)
+            if m.bias is not None:
+                m.bias.zero_()
+        elif isinstance(m, (nn.BatchNorm2d, nn.BatchNorm1d)):
+            c = m.num_features
+            m.weight.copy_(torch.rand(c, generator=g) * 0.4 + 0.8)
+            m.bias.copy_(torch.randn(c, generator=g) * 0.1)
+            m.running_mean.copy_(torch.randn(c, generator=g) * 0.1)
+            m.running_var.copy_(torch.rand(c, generator=g) + 0.5)
+        elif isinstance(m, nn.Linear):
+            bound = 1.0 / m.in_features ** 0.5
+            m.weight.copy_((torch.rand(m.weight.shape, generator=g) * 2 - 1) * bound)
+            if m.bias is not None:
+                m.bias.copy_((torch.rand(m.bias.shape, generator=g) * 2 - 1) * bound)
+    return net
+
+
+@torch.no_grad()
+def calibrate_bn_(net: nn.Module, x_seq: torch.Tensor) -> nn.Module:
+    """Set every BatchNorm's running statistics to the batch statistics of one
+    forward over ``x_seq`` (what training would converge to), keeping its
+    affine gamma/beta.  With random weights and random BN statistics the
+    spiking activity of a deep SNN dies out after a few layers; calibrated
+    statistics keep per-layer firing rates in the range of a trained network,
+    so benchmarks exercise representative (dense) work."""
+    bns = [m for m in net.modules() if isinstance(m, (nn.BatchNorm2d, nn.BatchNorm1d))]
+    saved = [(m.momentum, m.training) for m in bns]
+    for m in bns:
+        m.momentum = 1.0
+        m.train()
+    functional.reset_net(net)
+    net(x_seq)
+    functional.reset_net(net)
+    for m, (mom, tr) in zip(bns, saved):
+        m.momentum = mom
+        m.train(tr)
+    return net

@@ -58,6 +58,7 @@ extern "C" {
 #define CF_RES_AND_POST  2  /* SEW 'AND' : out = identity * s               */
 #define CF_RES_IAND_POST 3  /* SEW 'IAND': out = identity * (1 - s)         */
 #define CF_RES_ADD_PRE   4  /* Spiking-ResNet: z += identity before the LIF */
+#define CF_RES_Z_ONLY    5  /* no LIF: out = BN(conv(x)) (a Conv+BN branch)  */
 
 /* ---- library / error ---------------------------------------------------- */
 CF_API const char* cf_version(void);
@@ -211,6 +212,12 @@ CF_API int cf_prescan_conv_tiles(const void* x, uint32_t* mask, int64_t* nnz_out
                           void* stream);
 /* Channel chunk the conv kernel uses for a given Cin_p in sparse mode. */
 CF_API int cf_conv_chunk(int64_t Cin_p, int sparse);
+
+/* Max pool (k, stride, pad; padding never wins) over x[B][H][W][T][C] fp16
+ * -> y[B][Ho][Wo][T][C].  The ResNet stem max-pool on spikes.  C % 8 == 0. */
+CF_API int cf_maxpool_bhwtc(const void* x, void* y, int64_t B, int64_t H, int64_t W,
+                            int64_t T, int64_t C, int64_t k, int64_t stride, int64_t pad,
+                            void* stream);
 
 /* ---- network head ---------------------------------------------------------- */
 

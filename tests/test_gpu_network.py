@@ -1,0 +1,197 @@
+"""GPU tests of the rewritten networks and the module-level patterns, called
+through the public API (optimize / patterns) and checked against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from lif_parity import check_lif_parity, lif_trace
+
+pytestmark = pytest.mark.gpu
+
+
+def _sew_net(B=8, seed=0):
+    from catfuse_b200.sj import zoo
+    net = zoo.init_random_(zoo.build_sew_resnet18_cifar(), seed)
+    g = torch.Generator().manual_seed(100 + seed)
+    x = torch.randn(B, 3, 32, 32, generator=g).unsqueeze(0).repeat(4, 1, 1, 1, 1)
+    zoo.calibrate_bn_(net, x)
+    return net.eval(), x
+
+
+def _teacher_forced_layers(plan, dev):
+    """Every fused conv layer of the plan checked against the oracle fed with
+    the plan's own input activation (fp16 operands, fp32 accumulation)."""
+    from catfuse_b200 import ops
+    from catfuse_b200.network import ConvStep
+    worst = 0.0
+    for st in plan.steps:
+        if not isinstance(st, ConvStep):
+            continue
+        spec = st.native.spec
+        C = plan.shapes[st.src][-1]
+        x = ops.unpack_bhwtc(plan.acts[st.src]).cpu()[:, :, :spec.in_channels]
+        y = ops.unpack_bhwtc(plan.acts[st.dst]).cpu().numpy()
+        w = st.native.params.weight.detach().float().cpu()
+        scale = None if st.scale is None else st.scale.cpu()
+        shift = None if st.shift is None else st.shift.cpu()
+        z = oracle.conv.conv_z(x, w, scale, shift, spec.stride, spec.padding,
+                               operand_dtype=torch.float16).numpy()
+        if st.lif is None:
+            assert np.abs(y - z).max() <= 2e-3 * max(1.0, np.abs(z).max()), st.name
+            continue
+        ident = None
+        if st.identity is not None:
+            ident = ops.unpack_bhwtc(plan.acts[st.identity]).cpu().numpy()
+        zz = z + ident if (ident is not None and st.res_mode == "add_pre") else z
+        s_o, v_o, h = lif_trace(zz.astype(np.float32))
+        out_o = s_o
+        if ident is not None and st.res_mode in ("ADD", "add"):
+            out_o = ident + s_o
+        v = ops.v_to_nchw(st.v).cpu().numpy()
+        s_got = y - ident if (ident is not None and st.res_mode in ("ADD", "add")) else y
+        rate = check_lif_parity(s_got, v, s_o, v_o, h, v_tol=1e-4, near_tol=1e-3,
+                                max_flip_rate=1e-4, what=st.name)
+        worst = max(worst, rate)
+    return worst
+
+
+def test_sew_resnet18_network_vs_oracle(dev):
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import functional
+    net, x = _sew_net()
+    params = {k: v.detach().float() for k, v in net.state_dict().items()}
+    model, stats = optimize(net, device=dev, T=4)
+    assert stats["native_plan"] and stats["fused_lif_nodes"] == stats["total_lif_nodes"] == 20
+    functional.reset_net(model)
+    logits = model(x.to(dev)).cpu()
+    plan = model.plan_for(x.to(dev))
+    _teacher_forced_layers(plan, dev)
+    ref = oracle.sew_resnet18_forward(x, params)
+    # independent fp32 end-to-end reference: close logits, same predictions
+    rel = (logits - ref).abs().max() / ref.abs().max()
+    assert rel < 5e-2, f"logits rel err {rel}"
+    agree = (logits.sum(0).argmax(-1) == ref.sum(0).argmax(-1)).float().mean()
+    assert agree >= 0.75, f"argmax agreement {agree}"
+
+
+def test_network_graph_eager_and_state_carry(dev):
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import functional
+    net, x = _sew_net(B=4, seed=1)
+    m_graph, _ = optimize(net, device=dev, T=4)
+    m_eager, _ = optimize(net, device=dev, T=4, use_graph=False)
+    xd = x.to(dev)
+    functional.reset_net(m_graph)
+    functional.reset_net(m_eager)
+    a = m_graph(xd)
+    b = m_eager(xd)
+    assert torch.equal(a, b)
+    # StateCarry: a second call without reset continues the membrane; equal to
+    # the last 4 steps of one T=8 call
+    a2 = m_graph(xd)
+    m8, _ = optimize(net, device=dev, T=8)
+    functional.reset_net(m8)
+    l8 = m8(torch.cat([xd, xd], 0))
+    assert torch.equal(a2, l8[4:])
+    assert torch.equal(a, l8[:4])
+    # reset -> identical to the first call
+    functional.reset_net(m_graph)
+    assert torch.equal(m_graph(xd), a)
+
+
+def test_spiking_resnet18_imagenet_small(dev):
+    """Standard Spiking ResNet (add before LIF, 7x7/2 stem + max-pool) at a
+    reduced 64x64 input."""
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import functional, zoo
+    net = zoo.init_random_(zoo.build_spiking_resnet18_imagenet(num_classes=100), 3)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 3, 64, 64, generator=g).unsqueeze(0).repeat(4, 1, 1, 1, 1)
+    zoo.calibrate_bn_(net, x)
+    net.eval()
+    params = {k: v.detach().float() for k, v in net.state_dict().items()}
+    model, stats = optimize(net, device=dev, T=4)
+    assert stats["native_plan"]
+    functional.reset_net(model)
+    logits = model(x.to(dev)).cpu()
+    ref = oracle.spiking_resnet18_forward(x, params)
+    rel = (logits - ref).abs().max() / ref.abs().max()
+    assert rel < 5e-2, f"logits rel err {rel}"
+
+
+def test_patterns_module_level(dev):
+    from catfuse_b200 import patterns
+    from catfuse_b200.sj import layer, neuron
+    import torch.nn as nn
+    g = torch.Generator().manual_seed(9)
+    conv = layer.Conv2d(32, 64, 3, 1, 1, bias=True)
+    bn = layer.BatchNorm2d(64)
+    with torch.no_grad():
+        conv.weight.copy_(torch.randn(conv.weight.shape, generator=g) * 0.15)
+        conv.bias.copy_(torch.randn(64, generator=g) * 0.1)
+        bn.running_mean.copy_(torch.randn(64, generator=g) * 0.1)
+        bn.running_var.copy_(torch.rand(64, generator=g) + 0.5)
+        bn.weight.copy_(torch.rand(64, generator=g) * 0.4 + 0.8)
+        bn.bias.copy_(torch.randn(64, generator=g) * 0.1)
+    bn.eval()
+    lif = neuron.LIFNode(tau=2.0, step_mode="m")
+    x = (torch.rand(4, 2, 32, 10, 10, generator=g) < 0.3).float()
+    scale, shift = oracle.fold_bn(bn.weight.detach(), bn.bias.detach(), bn.running_mean, bn.running_var)
+    shift_b = shift + conv.bias.detach() * scale
+    for cls in (patterns.PartialFusionConvBNLIF, patterns.STFusionConvBNLIF):
+        m = cls.from_sj_modules(conv, bn, lif).to(dev)
+        s1 = m(x.to(dev)).cpu().numpy()
+        s2 = m(x.to(dev)).cpu().numpy()   # v carried across calls
+        v2 = m.state.tensor.cpu().numpy()
+        s_o, v_o, z = oracle.conv_bn_lif(torch.cat([x, x]), conv.weight.detach(), scale, shift_b, 1, 1,
+                                         operand_dtype=torch.float16, return_z=True)
+        _, _, h = lif_trace(z)
+        check_lif_parity(np.concatenate([s1, s2]), v2, s_o, v_o, h, what=cls.__name__)
+        m.reset()
+        assert np.array_equal(m(x.to(dev)).cpu().numpy(), s1)
+    # STFusion: host-side EGD and device-side dispatch agree bit for bit
+    st = patterns.STFusionConvBNLIF.from_sj_modules(conv, bn, lif).to(dev)
+    xs = x.clone()
+    xs[:, :, :, :5] = 0
+    a = st(xs.to(dev))
+    st.reset()
+    st.egd = "host"
+    b = st(xs.to(dev))
+    assert torch.equal(a, b) and st.last_dispatch in ("SparseFlow", "DenseKeep")
+    st.reset()
+    z0 = st(torch.zeros_like(xs).to(dev))
+    assert st.last_dispatch == "StaticZero"
+    s_o, _ = oracle.lif_multistep(np.broadcast_to(shift_b.numpy()[None, None, :, None, None],
+                                                  (4, 2, 64, 10, 10)).astype(np.float32))
+    assert np.array_equal(z0.cpu().numpy(), s_o)
+
+
+def test_linear_lif_and_bn_add_lif(dev):
+    from catfuse_b200 import patterns
+    from catfuse_b200.sj import layer, neuron
+    g = torch.Generator().manual_seed(10)
+    lin = layer.Linear(96, 64)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(64, 96, generator=g) * 0.2)
+        lin.bias.copy_(torch.randn(64, generator=g) * 0.2)
+    lif = neuron.LIFNode()
+    x = torch.randn(4, 3, 5, 96, generator=g)    # [T, B, tokens, C]
+    m = patterns.FusedLinearLIF.from_sj_modules(lin, lif).to(dev)
+    s = m(x.to(dev)).cpu().numpy()
+    z = (x.half().float() @ lin.weight.detach().half().float().T + lin.bias.detach()).numpy()
+    s_o, v_o, h = lif_trace(z)
+    check_lif_parity(s, None, s_o, None, h, near_tol=2e-3, what="linear_lif")
+    # Conv-BN-Add-LIF (Spiking ResNet second half)
+    conv = layer.Conv2d(32, 32, 3, 1, 1, bias=False)
+    bn = layer.BatchNorm2d(32).eval()
+    with torch.no_grad():
+        conv.weight.copy_(torch.randn(conv.weight.shape, generator=g) * 0.2)
+    pat = patterns.PartialFusionConvBNAddLIF.from_sj_modules(conv, bn, lif).to(dev)
+    xs = (torch.rand(4, 2, 32, 8, 8, generator=g) < 0.3).float()
+    ident = torch.randn(4, 2, 32, 8, 8, generator=g).half().float()
+    out = pat(xs.to(dev), ident.to(dev)).cpu().numpy()
+    scale, shift = oracle.fold_bn(bn.weight.detach(), bn.bias.detach(), bn.running_mean, bn.running_var)
+    z = oracle.conv.conv_z(xs, conv.weight.detach(), scale, shift, 1, 1, operand_dtype=torch.float16).numpy()
+    s_o, v_o, h = lif_trace((z + ident.numpy()).astype(np.float32))
+    check_lif_parity(out, None, s_o, None, h, what="conv_bn_add_lif")
