@@ -259,7 +259,7 @@ def main():
     for _ in range(3):
         plan.fresh = True
         ev = []
-        ops.pack_tbchw(plan.x_in, plan.shapes[0][-1], out=plan.acts[0])
+        plan.pack_input()
         for st in plan.steps:
             if not isinstance(st, ConvStep):
                 continue
@@ -270,7 +270,7 @@ def main():
             flush.fill_(1.0)
             a.record()
             mode = "z_only" if st.lif is None else (st.res_mode if ident is not None else "none")
-            ops.conv_bn_lif(plan.acts[st.src], st.wp, st.scale, st.shift, spec.stride, spec.padding,
+            ops.conv_bn_lif(plan.acts[st.src], st.wp, st.scale, st.shift, st.stride, st.pad,
                             identity=ident if st.lif is not None else None, res_mode=mode,
                             v_in=None, v_out=st.v, lif=st.lif or ops.LIFConfig(),
                             out=plan.acts[st.dst])

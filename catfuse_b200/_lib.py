@@ -42,6 +42,7 @@ SIGNATURES = {
     "cf_avgpool_lif": (_INT, [_P, _P, _P, _INT, _P, _I64, _I64, _I64, _I64, _I64, _INT, _F, _F,
                               _F, _INT, _INT, _P]),
     "cf_pack_tbchw": (_INT, [_P, _INT, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "cf_pack_im2col": (_INT, [_P, _INT, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "cf_unpack_bhwtc": (_INT, [_P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P]),
     "cf_v_layout": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _INT, _P]),
     "cf_pack_conv_weight": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
@@ -56,6 +57,7 @@ SIGNATURES = {
                                      _I64, _I64, _I64, _P]),
     "cf_conv_chunk": (_INT, [_I64, _INT]),
     "cf_maxpool_bhwtc": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
+    "cf_debug_read_trace": (_INT, [ctypes.POINTER(ctypes.c_longlong), _INT]),
     "cf_avgpool_fc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
 }
 

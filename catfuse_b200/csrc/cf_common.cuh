@@ -108,6 +108,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Non-blocking probe of an mbarrier phase (no thread suspension).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -212,6 +225,16 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t row_
   d |= (uint64_t)(((8u * row_bytes) >> 4) & 0x3FFFu) << 32;  // stride byte offset
   d |= (uint64_t)1 << 46;                             // descriptor version (sm100)
   d |= layout << 61;                                  // swizzle mode
+  return d;
+}
+
+// As make_smem_desc, but for a 128-byte-swizzled operand that may start at
+// any row of a 1024-byte-aligned swizzle pattern: the descriptor's base-offset
+// field carries the starting row within the 8-row pattern.
+__device__ __forceinline__ uint64_t make_smem_desc_rows(uint32_t saddr, uint32_t row_bytes,
+                                                        bool base_off) {
+  uint64_t d = make_smem_desc(saddr, row_bytes);
+  if (base_off && row_bytes == 128) d |= (uint64_t)((saddr >> 7) & 7u) << 49;
   return d;
 }
 

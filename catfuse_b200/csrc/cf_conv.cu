@@ -18,9 +18,11 @@
 // spikes (fp16, optionally combined with a SEW identity) and the final
 // membrane.  Neither z nor the per-step v ever reaches global memory.
 //
-// Warp roles (192 threads, one persistent CTA per SM):
-//   warp 0     TMA producer          warp 1     MMA issuer + TMEM owner
-//   warps 2-5  epilogue (TMEM lane quarter = warp % 4)
+// Warp roles (416 threads, one persistent CTA per SM):
+//   warps 0-3   TMA producers (a TMA instruction occupies its issuing thread
+//               for hundreds of cycles, so four threads issue in parallel)
+//   warp 4      MMA issuer + TMEM owner
+//   warps 5-12  epilogue (TMEM lane quarter = warp % 4, two warps per quarter)
 // The accumulator is double-buffered in TMEM so the epilogue of tile i
 // overlaps the main loop of tile i+1.
 //
@@ -33,6 +35,7 @@
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <mutex>
 
 namespace cf {
@@ -41,11 +44,20 @@ namespace cf {
 // code of the first expiry.  Read and cleared by cf_check_device_error.
 __device__ int32_t g_dev_error = 0;
 
+// Tuning trace (CATFUSE_CONV_DEBUG bit 8): CTA 0 records clock64() stamps of
+// its first k-iterations: [0,256) producer issue, [256,512) MMA full-wait
+// done, [512,768) load-complete observed by producer-side poll (unused).
+__device__ long long g_trace[1024];
+
 namespace {
 
-constexpr int kConvThreads = 192;
+constexpr int kProdWarps = 4;  // a TMA instruction holds its issuing thread for ~400 cycles
+constexpr int kMmaWarp = kProdWarps;
+constexpr int kEpiWarp0 = kProdWarps + 1;
+constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter
+constexpr int kConvThreads = 32 * (kProdWarps + 1 + kEpiWarps);
 constexpr int kEpiRowStride = 36;  // floats per transpose row (bank-conflict free)
-constexpr int kEpiBytes = 4 * 32 * kEpiRowStride * 4;
+constexpr int kEpiBytes = kEpiWarps * 32 * kEpiRowStride * 4;
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kMaxTP = 8;  // time steps per launch; longer T runs in blocks of 8
 
@@ -64,17 +76,31 @@ struct ConvArgs {
   int KH, KW, stride, pad;
   int Wb, Hb, Bb;
   int n_wt, n_ht, n_mtiles, n_ntiles, n_tiles;
+  int BN, BK;       // N tile (output channels), K chunk (input channels)
   int n_kc;         // channel chunks per tap
   uint32_t kc_all;  // mask with n_kc low bits set
-  int res_mode;
+  uint32_t idesc;   // tcgen05 instruction descriptor (M=128, N=BN)
+  uint32_t tmem_cols;
   int stages;
+  int debug;        // tuning experiments only: bit0 = skip MMAs, bit1 = skip epilogue math
+  int nprod;        // producer threads in use (<= stages)
+  int wres;         // 1: the whole weight slab of the (single) N tile stays in shared memory
+  int halo;         // 1: one TMA box per tile carries the whole receptive field (all taps)
+  int Wh;           // halo box width (Wb + KW - 1)
+  int a_bytes;      // bytes of one activation stage
+  int boff;         // set the descriptor base offset for row-shifted operands
   LifParams lp;
 };
+
+#ifndef CF_SPIN_POLL
+#define CF_SPIN_POLL 0
+#endif
+constexpr bool kSpinPoll = CF_SPIN_POLL;
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int32_t site,
                                               volatile int* abort_flag) {
   for (uint32_t i = 0; i < kMaxPolls; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (kSpinPoll ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 255u && *abort_flag) return false;
   }
   atomicCAS(&g_dev_error, 0, site);
@@ -82,35 +108,168 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
   return false;
 }
 
+// Starting point of a tile's (tap, channel chunk) walk.  A tile-dependent
+// rotation (to spread concurrent weight fetches over L2 slices) measured
+// slower than the plain order, which keeps neighbouring SMs on the same
+// weight lines; kept as a hook.
+__device__ __forceinline__ int tile_rotation(int mt, int nt, int n_all) {
+  (void)mt; (void)nt; (void)n_all;
+  return 0;
+}
+
 __device__ __forceinline__ uint32_t tile_kmask(const ConvArgs& a, int mt) {
   return a.tile_mask ? (__ldg(a.tile_mask + mt) & a.kc_all) : a.kc_all;
 }
 
-template <int BN, int BK, int TP>
+// LIF step for the common configuration (decay_input, hard reset, tau a power
+// of two).  (z - (v - v_reset)) * (1/tau) is exact there, so the fused
+// multiply-add rounds exactly once, like the separately rounded form.
+__device__ __forceinline__ float lif_step_fast(float& v, float z, const LifParams& p) {
+  const float h = fmaf(__fsub_rn(z, __fsub_rn(v, p.v_reset)), p.rtau, v);
+  const bool s = h >= p.v_th;
+  v = s ? p.v_reset : h;
+  return s ? 1.0f : 0.0f;
+}
+
+template <bool FAST>
+__device__ __forceinline__ float lif_any(float& v, float z, const LifParams& p) {
+  if constexpr (FAST) return lif_step_fast(v, z, p);
+  else return lif_step(v, z, p);
+}
+
+// Epilogue of one 32-row x 32-column accumulator block held (row-major,
+// stride kEpiRowStride) in this warp's transpose buffer.  Lane (pp, cs) owns
+// pixel pp of the warp and channels [cs*CW, cs*CW+CW) for all TP steps.
+template <int TP, int RES, bool FAST>
+__device__ __forceinline__ void epi_block(const ConvArgs& a, const float* epi, int pp, int cs,
+                                          bool pix_ok, int64_t pix, int col0) {
+  constexpr int CW = 32 / TP;
+  float sc[CW], sh[CW], v[CW];
+#pragma unroll
+  for (int j = 0; j < CW; j += 4) {
+    const float4 s4 = a.scale ? __ldg(reinterpret_cast<const float4*>(a.scale + col0 + j))
+                              : make_float4(1.f, 1.f, 1.f, 1.f);
+    const float4 h4 = a.shift ? __ldg(reinterpret_cast<const float4*>(a.shift + col0 + j))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+    sc[j] = s4.x; sc[j + 1] = s4.y; sc[j + 2] = s4.z; sc[j + 3] = s4.w;
+    sh[j] = h4.x; sh[j + 1] = h4.y; sh[j + 2] = h4.z; sh[j + 3] = h4.w;
+  }
+  if (RES != CF_RES_Z_ONLY && a.v_in && pix_ok) {
+    const float4* vp = reinterpret_cast<const float4*>(a.v_in + pix * a.Cout + col0);
+#pragma unroll
+    for (int j = 0; j < CW / 4; ++j) {
+      const float4 t4 = vp[j];
+      v[4 * j] = t4.x; v[4 * j + 1] = t4.y; v[4 * j + 2] = t4.z; v[4 * j + 3] = t4.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = 0.f;
+  }
+  constexpr bool kIdent = (RES != CF_RES_NONE && RES != CF_RES_Z_ONLY);
+  float idv[kIdent ? TP : 1][CW];
+  if constexpr (kIdent) {
+    // All steps' identity loads are independent: issue them before the recurrence.
+#pragma unroll
+    for (int t = 0; t < TP; ++t) {
+      if (t < a.tcount && pix_ok) {
+        const int64_t row = (pix * a.T + a.t0 + t) * a.Cout + col0;
+        const __half2* ip = reinterpret_cast<const __half2*>(a.identity + row);
+#pragma unroll
+        for (int j = 0; j < CW / 2; ++j) {
+          const float2 f = __half22float2(ip[j]);
+          idv[t][2 * j] = f.x; idv[t][2 * j + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) idv[t][j] = 0.f;
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < TP; ++t) {
+    if (t < a.tcount) {
+      float z[CW];
+      const float4* src =
+          reinterpret_cast<const float4*>(epi + (pp * TP + t) * kEpiRowStride + cs * CW);
+#pragma unroll
+      for (int j = 0; j < CW / 4; ++j) {
+        const float4 t4 = src[j];
+        z[4 * j] = t4.x; z[4 * j + 1] = t4.y; z[4 * j + 2] = t4.z; z[4 * j + 3] = t4.w;
+      }
+      __half2 o[CW / 2];
+#pragma unroll
+      for (int j = 0; j < CW; j += 2) {
+        float zz0 = fmaf(z[j], sc[j], sh[j]);
+        float zz1 = fmaf(z[j + 1], sc[j + 1], sh[j + 1]);
+        if constexpr (RES == CF_RES_ADD_PRE) {
+          zz0 = __fadd_rn(zz0, idv[t][j]);
+          zz1 = __fadd_rn(zz1, idv[t][j + 1]);
+        }
+        if constexpr (RES == CF_RES_Z_ONLY) {
+          o[j / 2] = __floats2half2_rn(zz0, zz1);
+        } else {
+          float s0 = lif_any<FAST>(v[j], zz0, a.lp);
+          float s1 = lif_any<FAST>(v[j + 1], zz1, a.lp);
+          if constexpr (RES == CF_RES_ADD_POST) {
+            s0 += idv[t][j]; s1 += idv[t][j + 1];
+          } else if constexpr (RES == CF_RES_AND_POST) {
+            s0 *= idv[t][j]; s1 *= idv[t][j + 1];
+          } else if constexpr (RES == CF_RES_IAND_POST) {
+            s0 = idv[t][j] * (1.f - s0); s1 = idv[t][j + 1] * (1.f - s1);
+          }
+          o[j / 2] = __floats2half2_rn(s0, s1);
+        }
+      }
+      if (pix_ok) {
+        const int64_t row = (pix * a.T + a.t0 + t) * a.Cout + col0;
+        if constexpr (CW >= 8) {
+          uint4* dst = reinterpret_cast<uint4*>(a.out + row);
+#pragma unroll
+          for (int j = 0; j < CW / 8; ++j) dst[j] = reinterpret_cast<const uint4*>(o)[j];
+        } else if constexpr (CW == 4) {
+          *reinterpret_cast<uint2*>(a.out + row) = *reinterpret_cast<const uint2*>(o);
+        } else {
+          *reinterpret_cast<uint32_t*>(a.out + row) = *reinterpret_cast<const uint32_t*>(o);
+        }
+      }
+    }
+  }
+  if (RES != CF_RES_Z_ONLY && a.v_out && pix_ok) {
+    float4* vp = reinterpret_cast<float4*>(a.v_out + pix * a.Cout + col0);
+#pragma unroll
+    for (int j = 0; j < CW / 4; ++j)
+      vp[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
+template <int TP, int RES, bool FAST>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_bn_lif_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const ConvArgs a) {
-  constexpr int A_BYTES = 128 * BK * 2;
-  constexpr int B_BYTES = BN * BK * 2;
-  constexpr int ROWB = BK * 2;  // bytes per operand row = swizzle width
-  constexpr int CW = 32 / TP;   // channels per lane after the transpose
   constexpr int PPW = 32 / TP;  // pixels per warp
-  constexpr uint32_t TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
-  constexpr uint32_t IDESC = make_idesc_f16(128, BN);
+  const int BN = a.BN, BK = a.BK;
+  const int A_BYTES = a.a_bytes;
+  const int B_BYTES = BN * BK * 2;
+  const uint32_t ROWB = (uint32_t)BK * 2;  // bytes per operand row = swizzle width
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int S = a.stages;
+  // Weight-resident mode: sB holds all KH*KW*n_kc weight blocks for good and
+  // the stages carry only activation tiles.
+  const int n_wblk = a.wres ? a.KH * a.KW * a.n_kc : S;
+  const int STAGE_B = a.wres ? 0 : B_BYTES;
   uint8_t* sA = smem;
   uint8_t* sB = sA + (size_t)S * A_BYTES;
-  float* sEpi = reinterpret_cast<float*>(sB + (size_t)S * B_BYTES);
+  float* sEpi = reinterpret_cast<float*>(sB + (size_t)n_wblk * B_BYTES);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sEpi) + kEpiBytes);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* done_bar = tempty_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  uint64_t* w_bar = done_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -123,18 +282,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], 4);
+      mbar_init(&tempty_bar[i], kEpiWarps);
     }
     mbar_init(done_bar, 1);
+    mbar_init(w_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp < kProdWarps && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, a.tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -142,12 +302,23 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued = 0;
+  if (warp < kProdWarps) {
+    // ------------------------------------------------------------ producers
+    // Producer p issues the loads of global k-iterations i with i % kProdWarps
+    // == p (stage i % S, phase (i / S) & 1); the MMA warp consumes in order.
+    if (lane == 0 && warp < a.nprod) {
+      const int p = warp;
+      if (a.wres && p == 0) {
+        // Load the weight slab once: block (tap, kc) at sB + (tap*n_kc + kc)*B_BYTES.
+        mbar_arrive_expect_tx(w_bar, (uint32_t)(n_wblk * B_BYTES));
+        for (int tap = 0; tap < a.KH * a.KW; ++tap)
+          for (int kc = 0; kc < a.n_kc; ++kc)
+            tma_load_2d(sB + (size_t)(tap * a.n_kc + kc) * B_BYTES, &tmB, w_bar,
+                        tap * a.Cin_p + kc * BK, 0);
+      }
+      uint32_t it = 0;          // global k-iteration counter (all producers)
+      uint32_t used = 0;        // stages this producer loaded into (bit s)
+      uint32_t used_phase = 0;  // phase of its latest load per stage (bit s)
       bool ok = true;
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int mt = tile / a.n_ntiles;
@@ -160,45 +331,52 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int b0 = bt * a.Bb;
         const uint32_t km = tile_kmask(a, mt);
         if (km == 0) continue;
-        for (int kh = 0; kh < a.KH && ok; ++kh) {
-          for (int kw = 0; kw < a.KW && ok; ++kw) {
-            const int tap = kh * a.KW + kw;
-            for (int kc = 0; kc < a.n_kc; ++kc) {
+        const int n_tg = a.halo ? 1 : a.KH * a.KW;  // halo: all taps in one box
+        const int n_all = n_tg * a.n_kc;
+        const int rot = tile_rotation(mt, nt, n_all);
+        for (int jj = 0; jj < n_all && ok; ++jj) {
+          {
+            const int idx = (jj + rot) % n_all;
+            const int tg = idx / a.n_kc, kc = idx - tg * a.n_kc;
+            const int tap = tg;
+            const int kh = a.halo ? 0 : tap / a.KW, kw = a.halo ? 0 : tap - (tap / a.KW) * a.KW;
+            {
               if (!((km >> kc) & 1u)) continue;
+              const uint32_t i = it++;
+              if ((int)(i % (uint32_t)a.nprod) != p) continue;
+              const int stage = (int)(i % (uint32_t)S);
+              const uint32_t phase = (i / (uint32_t)S) & 1u;
               if (!wait_or_abort(&empty_bar[stage], phase ^ 1u, ERR_SITE_PRODUCER_EMPTY,
                                  abort_flag)) {
                 ok = false;
                 break;
               }
-              mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
+              if ((a.debug & 8) && blockIdx.x == 0 && i < 256) g_trace[i] = clock64();
+              mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + STAGE_B);
               tma_load_5d(sA + (size_t)stage * A_BYTES, &tmA, &full_bar[stage], kc * BK, a.t0,
                           wi0 + kw, hi0 + kh, b0);
-              tma_load_2d(sB + (size_t)stage * B_BYTES, &tmB, &full_bar[stage],
-                          tap * a.Cin_p + kc * BK, nt * BN);
-              ++issued;
-              if (++stage == S) {
-                stage = 0;
-                phase ^= 1u;
-              }
+              if (!a.wres)
+                tma_load_2d(sB + (size_t)stage * B_BYTES, &tmB, &full_bar[stage],
+                            tap * a.Cin_p + kc * BK, nt * BN);
+              used |= 1u << stage;
+              used_phase = (used_phase & ~(1u << stage)) | (phase << stage);
             }
           }
         }
       }
-      // Drain: wait (bounded) until the last loads issued have landed so no
-      // bulk copy is still writing this CTA's shared memory when it exits.
-      const uint32_t outstanding = issued < (uint32_t)S ? issued : (uint32_t)S;
-      for (uint32_t i = 0; i < outstanding; ++i) {
-        if (stage == 0) {
-          stage = S - 1;
-          phase ^= 1u;
-        } else {
-          --stage;
+      // On a normal exit every load was consumed by the MMA warp, which
+      // finishes before the final barrier.  After an abort, wait (bounded)
+      // for this producer's loads so no bulk copy still writes this CTA's
+      // shared memory when it exits.
+      if (!ok) {
+        for (int st = 0; st < S; ++st) {
+          if (!((used >> st) & 1u)) continue;
+          for (uint32_t q = 0; q < (1u << 16); ++q)
+            if (mbar_try_wait(&full_bar[st], (used_phase >> st) & 1u)) break;
         }
-        for (uint32_t p = 0; p < kMaxPolls; ++p)
-          if (mbar_try_wait(&full_bar[stage], phase)) break;
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int stage = 0;
@@ -206,10 +384,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      const int ksteps = BK / 16;
+      bool w_ready = false;
+      int mma_it = 0;
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int mt = tile / a.n_ntiles;
         const uint32_t km = tile_kmask(a, mt);
-        const int count = a.KH * a.KW * __popc(km);
+        const int count = __popc(km);
         if (!wait_or_abort(&tempty_bar[acc], acc_phase ^ 1u, ERR_SITE_MMA_TEMPTY, abort_flag)) {
           ok = false;
           break;
@@ -219,23 +400,54 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           mbar_arrive(&tfull_bar[acc]);
         } else {
           const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-          for (int i = 0; i < count; ++i) {
-            if (!wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag)) {
+          if (a.wres && !w_ready) {
+            if (!wait_or_abort(w_bar, 0, ERR_SITE_MMA_FULL, abort_flag)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t a_base = smem_u32(sA + (size_t)stage * A_BYTES);
-            const uint32_t b_base = smem_u32(sB + (size_t)stage * B_BYTES);
-#pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              umma_f16(d_tmem, make_smem_desc(a_base + kk * 32, ROWB),
-                       make_smem_desc(b_base + kk * 32, ROWB), IDESC, (i | kk) != 0 ? 1u : 0u);
-            }
-            umma_commit(&empty_bar[stage]);
-            if (++stage == S) {
-              stage = 0;
-              phase ^= 1u;
+            w_ready = true;
+          }
+          bool accum = false;
+          const int n_tg = a.halo ? 1 : a.KH * a.KW;
+          const int taps_per = a.halo ? a.KH * a.KW : 1;
+          const int n_all = n_tg * a.n_kc;
+          const int nt = tile - mt * a.n_ntiles;
+          const int rot = tile_rotation(mt, nt, n_all);
+          for (int jj = 0; jj < n_all && ok; ++jj) {
+            const int idx = (jj + rot) % n_all;
+            const int tg = idx / a.n_kc, kc = idx - tg * a.n_kc;
+            {
+              if (!((km >> kc) & 1u)) continue;
+              if (!wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag)) {
+                ok = false;
+                break;
+              }
+              if ((a.debug & 8) && blockIdx.x == 0 && mma_it < 256) g_trace[256 + mma_it] = clock64();
+              ++mma_it;
+              // No tcgen05 fence here: the mbarrier completion already orders
+              // the TMA writes before the MMA reads, and a fence per stage
+              // would serialise consecutive MMAs.
+              const uint32_t a_stage = smem_u32(sA + (size_t)stage * A_BYTES);
+              for (int j = 0; j < taps_per; ++j) {
+                const int tap = a.halo ? j : tg;
+                // halo: the tap's operand rows start (kh*Wh + kw)*TP rows into the box
+                const uint32_t a_base =
+                    a_stage + (a.halo ? (uint32_t)(((tap / a.KW) * a.Wh + tap % a.KW) * TP) * ROWB
+                                      : 0u);
+                const uint32_t b_base =
+                    smem_u32(sB + (size_t)(a.wres ? tap * a.n_kc + kc : stage) * B_BYTES);
+                for (int kk = 0; kk < ksteps && !(a.debug & 1); ++kk) {
+                  umma_f16(d_tmem, make_smem_desc_rows(a_base + kk * 32, ROWB, a.boff),
+                           make_smem_desc(b_base + kk * 32, ROWB), a.idesc, accum ? 1u : 0u);
+                  accum = true;
+                }
+              }
+              if (a.debug & 4) mbar_arrive(&empty_bar[stage]);
+              else umma_commit(&empty_bar[stage]);
+              if (++stage == S) {
+                stage = 0;
+                phase ^= 1u;
+              }
             }
           }
           if (!ok) break;
@@ -251,14 +463,17 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter of this warp
-    float* epi = sEpi + q * 32 * kEpiRowStride;
+    const int e = warp - kEpiWarp0;  // 0..kEpiWarps-1
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int half = e / 4;          // which 32-column blocks this warp takes
+    float* epi = sEpi + e * 32 * kEpiRowStride;
     const int pp = lane / TP;       // pixel of this lane within the warp's rows
     const int cs = lane - pp * TP;  // channel sub-block of this lane
     const int pix_in_tile = q * PPW + pp;
     const int wb = pix_in_tile % a.Wb;
     const int hb = (pix_in_tile / a.Wb) % a.Hb;
     const int bb = pix_in_tile / (a.Wb * a.Hb);
+    const int nblk = BN / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
@@ -268,7 +483,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const int ht = (mt / a.n_wt) % a.n_ht;
       const int bt = mt / (a.n_wt * a.n_ht);
       const bool has_acc = tile_kmask(a, mt) != 0;
-      if (!wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag)) break;
+      // One lane polls the barrier (32 polling lanes per warp would flood the
+      // shared-memory pipe that the TMA writes go through); the others follow.
+      int got = 1;
+      if (lane == 0) got = wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
       tc_fence_after();
 
       const int wo = wt * a.Wb + wb;
@@ -276,9 +496,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const int b = bt * a.Bb + bb;
       const bool pix_ok = (wo < a.Wo) && (ho < a.Ho) && (b < a.B);
       const int64_t pix = ((int64_t)b * a.Ho + ho) * a.Wo + wo;
-
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
+      // This warp's column blocks are half, half+2, ...; after reading the
+      // last of them it releases the accumulator (one arrival per warp).
+      int last = -1;
+      for (int ch = half; ch < nblk; ch += 2) last = ch;
+      if (last < 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      }
+      for (int ch = half; ch < nblk; ch += 2) {
         float r[32];
         if (has_acc) {
           tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), r);
@@ -286,105 +512,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = 0.f;
         }
-        if (ch == BN / 32 - 1) {
-          // Accumulator fully read: hand the TMEM buffer back to the MMA warp.
+        if (ch == last) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty_bar[acc]);
         }
-        // Transpose the 32(rows) x 32(cols) block through shared memory.
         float4* row4 = reinterpret_cast<float4*>(epi + lane * kEpiRowStride);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) row4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        for (int j = 0; j < 8; ++j)
+          row4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
         __syncwarp();
-
-        const int col0 = nt * BN + ch * 32 + cs * CW;
-        float sc[CW], sh[CW], v[CW];
-#pragma unroll
-        for (int j = 0; j < CW; ++j) {
-          sc[j] = a.scale ? __ldg(a.scale + col0 + j) : 1.f;
-          sh[j] = a.shift ? __ldg(a.shift + col0 + j) : 0.f;
-        }
-        if (a.v_in && pix_ok) {
-          const float4* vp = reinterpret_cast<const float4*>(a.v_in + pix * a.Cout + col0);
-#pragma unroll
-          for (int j = 0; j < CW / 4; ++j) {
-            const float4 t4 = vp[j];
-            v[4 * j] = t4.x; v[4 * j + 1] = t4.y; v[4 * j + 2] = t4.z; v[4 * j + 3] = t4.w;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < CW; ++j) v[j] = 0.f;
-        }
-
-#pragma unroll
-        for (int t = 0; t < TP; ++t) {
-          if (t < a.tcount) {
-            float z[CW];
-            const float4* src =
-                reinterpret_cast<const float4*>(epi + (pp * TP + t) * kEpiRowStride + cs * CW);
-#pragma unroll
-            for (int j = 0; j < CW / 4; ++j) {
-              const float4 t4 = src[j];
-              z[4 * j] = t4.x; z[4 * j + 1] = t4.y; z[4 * j + 2] = t4.z; z[4 * j + 3] = t4.w;
-            }
-            const int64_t row = (pix * a.T + a.t0 + t) * a.Cout + col0;
-            float idv[CW];
-            if (a.res_mode != CF_RES_NONE && a.res_mode != CF_RES_Z_ONLY && pix_ok) {
-              const __half2* ip = reinterpret_cast<const __half2*>(a.identity + row);
-#pragma unroll
-              for (int j = 0; j < CW / 2; ++j) {
-                const float2 f = __half22float2(ip[j]);
-                idv[2 * j] = f.x; idv[2 * j + 1] = f.y;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < CW; ++j) idv[j] = 0.f;
-            }
-            __half2 o[CW / 2];
-#pragma unroll
-            for (int j = 0; j < CW; j += 2) {
-              float zz0 = __fadd_rn(__fmul_rn(z[j], sc[j]), sh[j]);
-              float zz1 = __fadd_rn(__fmul_rn(z[j + 1], sc[j + 1]), sh[j + 1]);
-              if (a.res_mode == CF_RES_ADD_PRE) {
-                zz0 = __fadd_rn(zz0, idv[j]);
-                zz1 = __fadd_rn(zz1, idv[j + 1]);
-              }
-              if (a.res_mode == CF_RES_Z_ONLY) {
-                o[j / 2] = __floats2half2_rn(zz0, zz1);
-                continue;
-              }
-              float s0 = lif_step(v[j], zz0, a.lp);
-              float s1 = lif_step(v[j + 1], zz1, a.lp);
-              if (a.res_mode == CF_RES_ADD_POST) {
-                s0 += idv[j]; s1 += idv[j + 1];
-              } else if (a.res_mode == CF_RES_AND_POST) {
-                s0 *= idv[j]; s1 *= idv[j + 1];
-              } else if (a.res_mode == CF_RES_IAND_POST) {
-                s0 = idv[j] * (1.f - s0); s1 = idv[j + 1] * (1.f - s1);
-              }
-              o[j / 2] = __floats2half2_rn(s0, s1);
-            }
-            if (pix_ok) {
-              if constexpr (CW >= 8) {
-                uint4* dst = reinterpret_cast<uint4*>(a.out + row);
-#pragma unroll
-                for (int j = 0; j < CW / 8; ++j) dst[j] = reinterpret_cast<const uint4*>(o)[j];
-              } else if constexpr (CW == 4) {
-                *reinterpret_cast<uint2*>(a.out + row) = *reinterpret_cast<const uint2*>(o);
-              } else {
-                *reinterpret_cast<uint32_t*>(a.out + row) = *reinterpret_cast<const uint32_t*>(o);
-              }
-            }
-          }
-        }
-        if (a.v_out && pix_ok && a.res_mode != CF_RES_Z_ONLY) {
-          float4* vp = reinterpret_cast<float4*>(a.v_out + pix * a.Cout + col0);
-#pragma unroll
-          for (int j = 0; j < CW / 4; ++j)
-            vp[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        }
-        __syncwarp();  // transpose buffer is reused by the next chunk
+        if (!(a.debug & 2))
+          epi_block<TP, RES, FAST>(a, epi, pp, cs, pix_ok, pix, nt * BN + ch * 32 + cs * (32 / TP));
+        __syncwarp();  // transpose buffer is reused by the next block
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
@@ -393,9 +533,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc(tmem_base, a.tmem_cols);
   }
 }
 
@@ -466,12 +606,15 @@ int sm_count() {
 }
 
 int choose_bn(int Cout, int n_mtiles) {
+  static const int env_bn = getenv("CATFUSE_CONV_BN") ? atoi(getenv("CATFUSE_CONV_BN")) : 0;
+  if (env_bn >= 32 && env_bn <= 256 && Cout % env_bn == 0) return env_bn;
   int bn = 128;
   while (bn > 32 && (Cout % bn != 0)) bn >>= 1;
   if (Cout % bn != 0) return 0;
-  // Prefer more, smaller tiles while the grid would not fill the SMs.
   const int sms = 148;
-  while (bn > 64 && (long)n_mtiles * (Cout / bn) < sms) bn >>= 1;
+  // N=256 halves the MMA instructions and the activation re-reads per output,
+  // worth it while the grid still covers most SMs.
+  if (Cout % 256 == 0 && (long)n_mtiles * (Cout / 256) >= (sms * 3) / 4) bn = 256;
   return bn;
 }
 
@@ -493,59 +636,64 @@ int make_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout, in
   return g.BN ? CF_OK : fail(CF_ERR_UNSUPPORTED, "Cout=%lld must be a multiple of 32", (long long)Cout);
 }
 
-template <int BN, int BK, int TP>
+template <int TP, int RES, bool FAST>
 int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, int grid,
                 cudaStream_t stream) {
-  constexpr int A_BYTES = 128 * BK * 2;
-  constexpr int B_BYTES = BN * BK * 2;
+  const int A_BYTES = args.a_bytes;
+  const int B_BYTES = args.BN * args.BK * 2;
   const int fixed = 1024 + kEpiBytes + 256;
-  int stages = (kSmemBudget - fixed) / (A_BYTES + B_BYTES);
+  const int wslab = args.wres ? args.KH * args.KW * args.n_kc * B_BYTES : 0;
+  const int per_stage = A_BYTES + (args.wres ? 0 : B_BYTES);
+  int stages = (kSmemBudget - fixed - wslab) / per_stage;
   if (stages > 8) stages = 8;
+  if (args.stages > 1 && args.stages < stages) stages = args.stages;  // tuning override
   if (stages < 2) return fail(CF_ERR_UNSUPPORTED, "conv tile does not fit shared memory");
   args.stages = stages;
-  int smem = fixed + stages * (A_BYTES + B_BYTES);
+  // A producer may run at most `stages` iterations ahead of the consumer
+  // safely only if there are no more producers than stages.
+  args.nprod = stages < kProdWarps ? stages : kProdWarps;
+  int smem = fixed + wslab + stages * per_stage;
   // Keep every TMEM-using CTA above half the SM's shared memory so that two
   // of them can never be co-resident and contend for TMEM columns.
   if (smem < 120 * 1024) smem = 120 * 1024;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(conv_bn_lif_kernel<BN, BK, TP>,
+    cudaError_t e = cudaFuncSetAttribute(conv_bn_lif_kernel<TP, RES, FAST>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(conv)");
     attr_set = true;
   }
-  conv_bn_lif_kernel<BN, BK, TP><<<grid, kConvThreads, smem, stream>>>(tmA, tmB, args);
+  conv_bn_lif_kernel<TP, RES, FAST><<<grid, kConvThreads, smem, stream>>>(tmA, tmB, args);
   return check_launch("conv_bn_lif launch");
 }
 
-template <int BN, int BK>
-int dispatch_tp(int TP, const CUtensorMap& A, const CUtensorMap& W, const ConvArgs& args, int grid,
-                cudaStream_t s) {
-  switch (TP) {
-    case 1: return launch_inst<BN, BK, 1>(A, W, args, grid, s);
-    case 2: return launch_inst<BN, BK, 2>(A, W, args, grid, s);
-    case 4: return launch_inst<BN, BK, 4>(A, W, args, grid, s);
-    default: return launch_inst<BN, BK, 8>(A, W, args, grid, s);
+template <int TP, int RES>
+int dispatch_fast(bool fast, const CUtensorMap& A, const CUtensorMap& W, const ConvArgs& args,
+                  int grid, cudaStream_t s) {
+  return fast ? launch_inst<TP, RES, true>(A, W, args, grid, s)
+              : launch_inst<TP, RES, false>(A, W, args, grid, s);
+}
+
+template <int TP>
+int dispatch_res(int res, bool fast, const CUtensorMap& A, const CUtensorMap& W,
+                 const ConvArgs& args, int grid, cudaStream_t s) {
+  switch (res) {
+    case CF_RES_NONE: return dispatch_fast<TP, CF_RES_NONE>(fast, A, W, args, grid, s);
+    case CF_RES_ADD_POST: return dispatch_fast<TP, CF_RES_ADD_POST>(fast, A, W, args, grid, s);
+    case CF_RES_AND_POST: return dispatch_fast<TP, CF_RES_AND_POST>(fast, A, W, args, grid, s);
+    case CF_RES_IAND_POST: return dispatch_fast<TP, CF_RES_IAND_POST>(fast, A, W, args, grid, s);
+    case CF_RES_ADD_PRE: return dispatch_fast<TP, CF_RES_ADD_PRE>(fast, A, W, args, grid, s);
+    default: return launch_inst<TP, CF_RES_Z_ONLY, true>(A, W, args, grid, s);
   }
 }
 
-template <int BN>
-int dispatch_bk(int BK, int TP, const CUtensorMap& A, const CUtensorMap& W, const ConvArgs& args,
-                int grid, cudaStream_t s) {
-  switch (BK) {
-    case 16: return dispatch_tp<BN, 16>(TP, A, W, args, grid, s);
-    case 32: return dispatch_tp<BN, 32>(TP, A, W, args, grid, s);
-    default: return dispatch_tp<BN, 64>(TP, A, W, args, grid, s);
-  }
-}
-
-int dispatch(const Geometry& g, const CUtensorMap& A, const CUtensorMap& W, const ConvArgs& args,
-             int grid, cudaStream_t s) {
-  switch (g.BN) {
-    case 32: return dispatch_bk<32>(g.BK, g.TP, A, W, args, grid, s);
-    case 64: return dispatch_bk<64>(g.BK, g.TP, A, W, args, grid, s);
-    case 128: return dispatch_bk<128>(g.BK, g.TP, A, W, args, grid, s);
-    default: return dispatch_bk<256>(g.BK, g.TP, A, W, args, grid, s);
+int dispatch(const Geometry& g, int res, bool fast, const CUtensorMap& A, const CUtensorMap& W,
+             const ConvArgs& args, int grid, cudaStream_t s) {
+  switch (g.TP) {
+    case 1: return dispatch_res<1>(res, fast, A, W, args, grid, s);
+    case 2: return dispatch_res<2>(res, fast, A, W, args, grid, s);
+    case 4: return dispatch_res<4>(res, fast, A, W, args, grid, s);
+    default: return dispatch_res<8>(res, fast, A, W, args, grid, s);
   }
 }
 
@@ -605,6 +753,20 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
 
   // A: x[B][H][W][T][Cin_p] fp16, 5-D, box (BK, TP, Wb*s, Hb*s, Bb) with
   // element stride s along W and H (the TMA then loads Wb x Hb elements).
+  // Weight residency: a single N tile whose whole weight slab fits stays in
+  // shared memory for the CTA's lifetime.  Halo mode (stride 1, tile = one
+  // full output row): one activation box per tile covers all taps.
+  static const int env_wres = getenv("CATFUSE_CONV_WRES") ? atoi(getenv("CATFUSE_CONV_WRES")) : 1;
+  static const int env_halo = getenv("CATFUSE_CONV_HALO") ? atoi(getenv("CATFUSE_CONV_HALO")) : 1;
+  static const int env_boff = getenv("CATFUSE_CONV_HALO_BOFF") ? atoi(getenv("CATFUSE_CONV_HALO_BOFF")) : 0;
+  const int64_t wslab = KH * KW * g.n_kc * (int64_t)g.BN * g.BK * 2;
+  const int wres = (env_wres && Cout == g.BN && wslab <= 80 * 1024) ? 1 : 0;
+  const int Wh = g.Wb + (int)KW - 1;
+  const int halo_bytes = ((g.TP * Wh * (int)KH * g.BK * 2) + 1023) / 1024 * 1024;
+  const int fixed_bytes = 1024 + kEpiBytes + 256;
+  const int halo = (env_halo && wres && stride == 1 && g.Hb == 1 && g.Bb == 1 &&
+                    g.Wb * g.TP == 128 && g.TP >= 4 && g.BK == 64 && Wh <= 256 && KH <= 256 &&
+                    fixed_bytes + wslab + 2 * halo_bytes <= kSmemBudget) ? 1 : 0;
   CUtensorMap tmA, tmB;
   {
     cuuint64_t dims[5] = {(cuuint64_t)Cin_p, (cuuint64_t)T, (cuuint64_t)W, (cuuint64_t)H,
@@ -613,6 +775,10 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
                              (cuuint64_t)(W * T * Cin_p * 2), (cuuint64_t)(H * W * T * Cin_p * 2)};
     cuuint32_t box[5] = {(cuuint32_t)g.BK, (cuuint32_t)g.TP, (cuuint32_t)(g.Wb * stride),
                          (cuuint32_t)(g.Hb * stride), (cuuint32_t)g.Bb};
+    if (halo) {
+      box[2] = (cuuint32_t)Wh;
+      box[3] = (cuuint32_t)KH;
+    }
     cuuint32_t estr[5] = {1, 1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
     CUresult r = encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(x), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(g.BK * 2),
@@ -647,8 +813,22 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.n_tiles = args.n_mtiles * args.n_ntiles;
   args.n_kc = g.n_kc;
   args.kc_all = g.n_kc >= 32 ? 0xFFFFFFFFu : ((1u << g.n_kc) - 1u);
-  args.res_mode = res_mode;
+  args.BN = g.BN;
+  args.BK = g.BK;
+  args.idesc = make_idesc_f16(128, g.BN);
+  args.tmem_cols = (uint32_t)(2 * g.BN < 32 ? 32 : 2 * g.BN);
   args.lp = make_lif(tau, v_th, v_reset, hard_reset, decay_input);
+  const bool fast = args.lp.decay_input && args.lp.hard_reset && args.lp.tau_pow2;
+  // Tuning overrides for experiments: CATFUSE_CONV_STAGES, CATFUSE_CONV_DEBUG.
+  static const int env_stages = getenv("CATFUSE_CONV_STAGES") ? atoi(getenv("CATFUSE_CONV_STAGES")) : 0;
+  static const int env_debug = getenv("CATFUSE_CONV_DEBUG") ? atoi(getenv("CATFUSE_CONV_DEBUG")) : 0;
+  args.stages = env_stages;
+  args.debug = env_debug;
+  args.wres = wres;
+  args.halo = halo;
+  args.Wh = Wh;
+  args.boff = env_boff;
+  args.a_bytes = halo ? halo_bytes : 128 * g.BK * 2;
   const int grid = args.n_tiles < sm_count() ? args.n_tiles : sm_count();
 
   for (int64_t t0 = 0; t0 < T; t0 += kMaxTP) {
@@ -656,7 +836,7 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
     args.tcount = (int)((T - t0) < kMaxTP ? (T - t0) : kMaxTP);
     args.v_in = (t0 == 0) ? v_in : v_out;
     args.v_out = v_out;
-    if (int rc = dispatch(g, tmA, tmB, args, grid, stream)) return rc;
+    if (int rc = dispatch(g, res_mode, fast, tmA, tmB, args, grid, stream)) return rc;
   }
   return CF_OK;
 }
@@ -684,6 +864,11 @@ int cf_check_device_error(void* stream, int32_t* code) {
     return fail(CF_ERR_DEVICE_TIMEOUT, "a bounded device-side wait expired (site %d)", v);
   }
   return CF_OK;
+}
+
+int cf_debug_read_trace(long long* host, int n) {
+  if (!host || n <= 0 || n > 1024) return fail(CF_ERR_INVALID_ARG, "bad trace request");
+  return check_cuda(cudaMemcpyFromSymbol(host, g_trace, n * sizeof(long long)), "read trace");
 }
 
 int cf_conv_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout, int32_t* out6) {

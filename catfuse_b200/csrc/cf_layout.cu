@@ -171,6 +171,33 @@ __global__ void maxpool_kernel(const __half* __restrict__ x, __half* __restrict_
   }
 }
 
+// im2col packing for a convolution with few input channels (the network stem):
+// y[b][ho][wo][t][q] = x[t][b][c][ho*s-p+kh][wo*s-p+kw] for q = (kh*k+kw)*C+c
+// (zero outside the image and for q >= k*k*C).
+__global__ void im2col_kernel(const void* __restrict__ x, int fmt, __half* __restrict__ y, int T,
+                              int B, int C, int H, int W, int Ho, int Wo, int k, int s, int p,
+                              int Kp) {
+  const int64_t n = (int64_t)B * Ho * Wo * T * Kp;
+  const int KK = k * k * C;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(i % Kp);
+    int64_t r = i / Kp;
+    const int t = (int)(r % T); r /= T;
+    const int wo = (int)(r % Wo); r /= Wo;
+    const int ho = (int)(r % Ho);
+    const int b = (int)(r / Ho);
+    float v = 0.f;
+    if (q < KK) {
+      const int c = q % C, tap = q / C;
+      const int ih = ho * s - p + tap / k, iw = wo * s - p + tap % k;
+      if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+        v = ld_f(x, fmt, ((((int64_t)t * B + b) * C + c) * H + ih) * W + iw);
+    }
+    y[i] = __float2half_rn(v);
+  }
+}
+
 }  // namespace
 }  // namespace cf
 
@@ -246,6 +273,25 @@ int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b, float* lo
       static_cast<const __half*>(x), fc_w, fc_b, logits, (int)T, (int)B, (int)(H * W), (int)C,
       (int)K);
   return check_launch("avgpool_fc launch");
+}
+
+int cf_pack_im2col(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C, int64_t H,
+                   int64_t W, int64_t k, int64_t stride, int64_t pad, int64_t Kp, void* stream) {
+  if (!x || !y) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (x_fmt != CF_FMT_F32 && x_fmt != CF_FMT_F16) return fail(CF_ERR_INVALID_ARG, "bad x_fmt");
+  if (T <= 0 || B <= 0 || C <= 0 || H <= 0 || W <= 0 || k <= 0 || stride <= 0 || pad < 0 ||
+      Kp < k * k * C || Kp % 16)
+    return fail(CF_ERR_INVALID_ARG, "bad im2col shape (Kp >= k*k*C, Kp %% 16 == 0)");
+  const int64_t Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
+  if (Ho <= 0 || Wo <= 0) return fail(CF_ERR_INVALID_ARG, "empty output map");
+  if (int rc = require_sm100()) return rc;
+  const int64_t n = B * Ho * Wo * T * Kp;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  im2col_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, x_fmt, static_cast<__half*>(y), (int)T, (int)B, (int)C, (int)H, (int)W, (int)Ho,
+      (int)Wo, (int)k, (int)stride, (int)pad, (int)Kp);
+  return check_launch("im2col launch");
 }
 
 int cf_maxpool_bhwtc(const void* x, void* y, int64_t B, int64_t H, int64_t W, int64_t T,

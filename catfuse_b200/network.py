@@ -50,6 +50,9 @@ class ConvStep:
     wp: Optional[torch.Tensor] = None
     scale: Optional[torch.Tensor] = None
     shift: Optional[torch.Tensor] = None
+    stride: int = 0               # launch geometry (differs from spec for im2col)
+    pad: int = 0
+    im2col: bool = False
 
 
 @dataclass
@@ -121,7 +124,17 @@ class NetworkPlan:
         cin = stem.in_channels
         self.in_channels = cin
         self.x_in = torch.zeros((T, B, cin, H, W), dtype=torch.float32, device=self.device)
-        self.shapes.append((B, H, W, T, ops.pad16(cin)))
+        sspec = _native_of(stem).spec
+        k0 = sspec.kernel_size
+        # A stem with few input channels runs as a 1x1 convolution over an
+        # im2col-packed input (one K chunk per tile instead of k*k taps).
+        self.im2col = k0 > 1 and cin * k0 * k0 <= 64
+        if self.im2col:
+            ho0, wo0 = sspec.output_hw(H, W)
+            self.shapes.append((B, ho0, wo0, T, ops.pad16(cin * k0 * k0)))
+        else:
+            self.shapes.append((B, H, W, T, ops.pad16(cin)))
+        self.stem_geom = (k0, sspec.stride, sspec.padding)
         cur = 0
 
         def add_conv(name, pat, src, identity=None, res_mode="none", lif=True):
@@ -136,7 +149,14 @@ class NetworkPlan:
                                        _lif_of(pat) if lif else None, sparse))
             return dst
 
-        cur = add_conv("stem", stem, cur)
+        if self.im2col:
+            b_, h_, w_, t_, c_ = self.shapes[0]
+            self.shapes.append((b_, h_, w_, t_, sspec.out_channels))
+            self.steps.append(ConvStep("stem", _native_of(stem), 0, 1, None, "none", _lif_of(stem),
+                                       False, stride=1, pad=0, im2col=True))
+            cur = 1
+        else:
+            cur = add_conv("stem", stem, cur)
         mp = getattr(model, "maxpool", None)
         if isinstance(mp, nn.MaxPool2d):
             k = mp.kernel_size if isinstance(mp.kernel_size, int) else mp.kernel_size[0]
@@ -175,6 +195,11 @@ class NetworkPlan:
         for st in self.steps:
             if isinstance(st, ConvStep):
                 st.wp, st.scale, st.shift = st.native.packed(self.device)
+                if st.im2col:
+                    st.wp = ops.im2col_weight(st.native.params.weight.detach().to(self.device),
+                                              self.shapes[0][-1])
+                else:
+                    st.stride, st.pad = st.native.spec.stride, st.native.spec.padding
                 b_, ho, wo, t_, co = self.shapes[st.dst]
                 if st.lif is not None:
                     st.v = torch.zeros((b_, ho, wo, co), dtype=torch.float32, device=self.device)
@@ -191,8 +216,15 @@ class NetworkPlan:
             n += 1 + (1 if isinstance(st, ConvStep) and st.sparse else 0)
         return n
 
+    def pack_input(self):
+        if self.im2col:
+            k, s_, p_ = self.stem_geom
+            ops.pack_im2col(self.x_in, k, s_, p_, self.shapes[0][-1], out=self.acts[0])
+        else:
+            ops.pack_tbchw(self.x_in, self.shapes[0][-1], out=self.acts[0])
+
     def run_eager(self, fresh: bool):
-        ops.pack_tbchw(self.x_in, self.shapes[0][-1], out=self.acts[0])
+        self.pack_input()
         for st in self.steps:
             if isinstance(st, PoolStep):
                 ops.maxpool_bhwtc(self.acts[st.src], st.k, st.s, st.p, out=self.acts[st.dst])
@@ -205,11 +237,11 @@ class NetworkPlan:
                                        mask_out=st.mask)
             ident = self.acts[st.identity] if st.identity is not None else None
             if st.lif is None:
-                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, spec.stride,
-                                spec.padding, res_mode="z_only", out=self.acts[st.dst])
+                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
+                                st.pad, res_mode="z_only", out=self.acts[st.dst])
             else:
-                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, spec.stride,
-                                spec.padding, identity=ident,
+                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
+                                st.pad, identity=ident,
                                 res_mode=st.res_mode if ident is not None else "none",
                                 v_in=None if fresh else st.v, v_out=st.v,
                                 tile_mask=st.mask if st.sparse else None, lif=st.lif,

@@ -18,7 +18,7 @@ from ._lib import (FMT_BITS, FMT_F16, FMT_F32, FMT_U8, RES_ADD_POST, RES_ADD_PRE
 
 __all__ = [
     "LIFConfig", "lif_fwd", "bn_lif", "add_lif", "avgpool_lif", "pack_tbchw", "unpack_bhwtc",
-    "v_to_nhwc", "v_to_nchw", "pack_conv_weight", "conv_bn_lif", "linear_bn_lif",
+    "v_to_nhwc", "v_to_nchw", "pack_im2col", "im2col_weight", "pack_conv_weight", "conv_bn_lif", "linear_bn_lif",
     "conv_geometry", "prescan", "prescan_conv_tiles", "conv_chunk", "avgpool_fc", "maxpool_bhwtc",
     "pad16", "SPIKE_FORMATS", "RES_MODES",
 ]
@@ -200,6 +200,32 @@ def pack_tbchw(x: torch.Tensor, Cp: Optional[int] = None, out: Optional[torch.Te
         _need(out, "out", torch.float16)
     _lib.call("cf_pack_tbchw", x.data_ptr(), _zfmt(x), out.data_ptr(), T, B, C, H, W, Cp, _stream())
     return out
+
+
+def pack_im2col(x: torch.Tensor, k: int, stride: int, pad: int, Kp: Optional[int] = None,
+                out: Optional[torch.Tensor] = None):
+    """x[T,B,C,H,W] -> im2col [B,Ho,Wo,T,Kp] fp16 (q = (kh*k+kw)*C + c)."""
+    _need(x, "x")
+    T, B, C, H, W = x.shape
+    Kp = pad16(k * k * C) if Kp is None else int(Kp)
+    Ho = (H + 2 * pad - k) // stride + 1
+    Wo = (W + 2 * pad - k) // stride + 1
+    if out is None:
+        out = torch.empty((B, Ho, Wo, T, Kp), dtype=torch.float16, device=x.device)
+    _lib.call("cf_pack_im2col", x.data_ptr(), _zfmt(x), out.data_ptr(), T, B, C, H, W, k, stride,
+              pad, Kp, _stream())
+    return out
+
+
+def im2col_weight(w: torch.Tensor, Kp: Optional[int] = None) -> torch.Tensor:
+    """w[Cout,Cin,k,k] -> [Cout,1,1,Kp] fp16 matching pack_im2col's q order
+    (one-time weight preparation)."""
+    Cout, Cin, kh, kw = w.shape
+    Kp = pad16(kh * kw * Cin) if Kp is None else int(Kp)
+    flat = w.detach().float().permute(0, 2, 3, 1).reshape(Cout, kh * kw * Cin)
+    out = torch.zeros((Cout, Kp), dtype=torch.float32, device=w.device)
+    out[:, :flat.shape[1]] = flat
+    return out.half().reshape(Cout, 1, 1, Kp).contiguous()
 
 
 def unpack_bhwtc(y: torch.Tensor, C: Optional[int] = None, dtype=torch.float32,

@@ -122,6 +122,14 @@ CF_API int cf_avgpool_lif(const float* x, const float* v0, void* spikes, int spi
  * C..Cp-1 zero-filled.  Cp >= C, Cp % 16 == 0. */
 CF_API int cf_pack_tbchw(const void* x, int x_fmt, void* y, int64_t T, int64_t B,
                   int64_t C, int64_t H, int64_t W, int64_t Cp, void* stream);
+/* im2col for a k x k convolution with few input channels (the stem):
+ * x[T][B][C][H][W] (fp32/fp16) -> y[B][Ho][Wo][T][Kp] fp16 with
+ * y[..][q] = x[t][b][c][ho*stride-pad+kh][wo*stride-pad+kw], q = (kh*k+kw)*C+c,
+ * zero outside the image and for q >= k*k*C.  The convolution then runs as a
+ * 1x1 convolution with Cin_p = Kp (one K chunk per tile instead of k*k). */
+CF_API int cf_pack_im2col(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C,
+                          int64_t H, int64_t W, int64_t k, int64_t stride, int64_t pad,
+                          int64_t Kp, void* stream);
 /* y[B][H][W][T][C] fp16 -> x[T][B][C][H][W] (fp32 or fp16). */
 CF_API int cf_unpack_bhwtc(const void* y, void* x, int x_fmt, int64_t T, int64_t B,
                     int64_t C, int64_t H, int64_t W, void* stream);
@@ -218,6 +226,10 @@ CF_API int cf_conv_chunk(int64_t Cin_p, int sparse);
 CF_API int cf_maxpool_bhwtc(const void* x, void* y, int64_t B, int64_t H, int64_t W,
                             int64_t T, int64_t C, int64_t k, int64_t stride, int64_t pad,
                             void* stream);
+
+/* Tuning aid: copies n (<= 1024) clock64 stamps recorded by the fused conv
+ * kernel when CATFUSE_CONV_DEBUG has bit 8 set (synchronous). */
+CF_API int cf_debug_read_trace(long long* host, int n);
 
 /* ---- network head ---------------------------------------------------------- */
 

@@ -79,7 +79,7 @@ def make_resnet18_params(num_classes=10, stem="cifar", seed=0, in_ch=3):
     return p
 
 
-def _resnet18_forward(x, p, sew, stem, record=None):
+def _resnet18_forward(x, p, sew, stem, record=None, branch_dtype=None):
     x = torch.as_tensor(x, dtype=torch.float32)
     if stem == "cifar":
         z = _conv_bn(x, p, "conv1", "bn1", 1, 1)
@@ -119,6 +119,8 @@ def _resnet18_forward(x, p, sew, stem, record=None):
             else:
                 ident = (_conv_bn(xin, p, pre + ".downsample.0", pre + ".downsample.1", stride, 0)
                          if has_ds else xin)
+                if has_ds and branch_dtype is not None:   # storage precision of the branch
+                    ident = ident.to(branch_dtype).float()
                 s2, v2 = _lif(z2 + ident)
                 if record is not None:
                     record.append((pre + ".sn2", s2, v2))
@@ -134,5 +136,7 @@ def sew_resnet18_forward(x, p, stem="cifar", record=None):
     return _resnet18_forward(x, p, True, stem, record)
 
 
-def spiking_resnet18_forward(x, p, stem="imagenet", record=None):
-    return _resnet18_forward(x, p, False, stem, record)
+def spiking_resnet18_forward(x, p, stem="imagenet", record=None, branch_dtype=None):
+    """``branch_dtype`` rounds the Conv-BN downsample branch to that type before
+    the residual add (to mirror a kernel that stores the branch in fp16)."""
+    return _resnet18_forward(x, p, False, stem, record, branch_dtype)

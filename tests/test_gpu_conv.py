@@ -54,6 +54,10 @@ SHAPES = [
     (12, 1, 32, 32, 5, 5, 3, 1, 1),
     (4, 2, 16, 64, 15, 15, 7, 2, 3),
     (4, 2, 512, 512, 4, 4, 3, 1, 1),
+    # one full output row per tile (single-box receptive-field loads)
+    (4, 2, 64, 64, 32, 32, 3, 1, 1),
+    (2, 2, 64, 64, 64, 64, 3, 1, 1),
+    (4, 3, 64, 32, 32, 32, 3, 1, 1),
 ]
 
 
