@@ -474,6 +474,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const int hb = (pix_in_tile / a.Wb) % a.Hb;
     const int bb = pix_in_tile / (a.Wb * a.Hb);
     const int nblk = BN / 32;
+    int ep_it = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
@@ -489,6 +490,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       if (lane == 0) got = wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag);
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
+      if ((a.debug & 8) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_it < 256)
+        g_trace[512 + ep_it] = clock64();
       tc_fence_after();
 
       const int wo = wt * a.Wb + wb;
@@ -506,7 +509,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       }
       for (int ch = half; ch < nblk; ch += 2) {
         float r[32];
-        if (has_acc) {
+        if (has_acc && !(a.debug & 16)) {
           tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), r);
         } else {
 #pragma unroll
@@ -526,6 +529,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           epi_block<TP, RES, FAST>(a, epi, pp, cs, pix_ok, pix, nt * BN + ch * 32 + cs * (32 / TP));
         __syncwarp();  // transpose buffer is reused by the next block
       }
+      if ((a.debug & 8) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_it < 256)
+        g_trace[768 + ep_it] = clock64();
+      ++ep_it;
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }

@@ -177,24 +177,34 @@ __global__ void maxpool_kernel(const __half* __restrict__ x, __half* __restrict_
 __global__ void im2col_kernel(const void* __restrict__ x, int fmt, __half* __restrict__ y, int T,
                               int B, int C, int H, int W, int Ho, int Wo, int k, int s, int p,
                               int Kp) {
-  const int64_t n = (int64_t)B * Ho * Wo * T * Kp;
+  // One thread per output (pixel, t) row: gathers its k*k*C values and writes
+  // the Kp-wide row with 16-byte stores.
+  const int64_t n = (int64_t)B * Ho * Wo * T;
   const int KK = k * k * C;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int q = (int)(i % Kp);
-    int64_t r = i / Kp;
+    int64_t r = i;
     const int t = (int)(r % T); r /= T;
     const int wo = (int)(r % Wo); r /= Wo;
     const int ho = (int)(r % Ho);
     const int b = (int)(r / Ho);
-    float v = 0.f;
-    if (q < KK) {
-      const int c = q % C, tap = q / C;
-      const int ih = ho * s - p + tap / k, iw = wo * s - p + tap % k;
-      if (ih >= 0 && ih < H && iw >= 0 && iw < W)
-        v = ld_f(x, fmt, ((((int64_t)t * B + b) * C + c) * H + ih) * W + iw);
+    uint4* dst = reinterpret_cast<uint4*>(y + i * Kp);
+    for (int q0 = 0; q0 < Kp; q0 += 8) {
+      __align__(16) __half h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int q = q0 + j;
+        float v = 0.f;
+        if (q < KK) {
+          const int c = q % C, tap = q / C;
+          const int ih = ho * s - p + tap / k, iw = wo * s - p + tap % k;
+          if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+            v = ld_f(x, fmt, ((((int64_t)t * B + b) * C + c) * H + ih) * W + iw);
+        }
+        h[j] = __float2half_rn(v);
+      }
+      dst[q0 / 8] = *reinterpret_cast<const uint4*>(h);
     }
-    y[i] = __float2half_rn(v);
   }
 }
 
@@ -285,7 +295,9 @@ int cf_pack_im2col(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int6
   const int64_t Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
   if (Ho <= 0 || Wo <= 0) return fail(CF_ERR_INVALID_ARG, "empty output map");
   if (int rc = require_sm100()) return rc;
-  const int64_t n = B * Ho * Wo * T * Kp;
+  if ((reinterpret_cast<uintptr_t>(y) & 15) != 0)
+    return fail(CF_ERR_UNSUPPORTED, "y must be 16-byte aligned");
+  const int64_t n = B * Ho * Wo * T;
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   im2col_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
