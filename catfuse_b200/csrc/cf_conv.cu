@@ -89,6 +89,7 @@ struct ConvArgs {
   int Wh;           // halo box width (Wb + KW - 1)
   int a_bytes;      // bytes of one activation stage
   int boff;         // set the descriptor base offset for row-shifted operands
+  int backoff;      // ns of sleep between polls for the non-critical waiters
   LifParams lp;
 };
 
@@ -98,10 +99,11 @@ struct ConvArgs {
 constexpr bool kSpinPoll = CF_SPIN_POLL;
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int32_t site,
-                                              volatile int* abort_flag) {
+                                              volatile int* abort_flag, int backoff_ns = 0) {
   for (uint32_t i = 0; i < kMaxPolls; ++i) {
     if (kSpinPoll ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 255u && *abort_flag) return false;
+    if (backoff_ns) __nanosleep(backoff_ns);
   }
   atomicCAS(&g_dev_error, 0, site);
   *abort_flag = 1;
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               const int stage = (int)(i % (uint32_t)S);
               const uint32_t phase = (i / (uint32_t)S) & 1u;
               if (!wait_or_abort(&empty_bar[stage], phase ^ 1u, ERR_SITE_PRODUCER_EMPTY,
-                                 abort_flag)) {
+                                 abort_flag, a.backoff)) {
                 ok = false;
                 break;
               }
@@ -436,7 +438,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                                       : 0u);
                 const uint32_t b_base =
                     smem_u32(sB + (size_t)(a.wres ? tap * a.n_kc + kc : stage) * B_BYTES);
-                for (int kk = 0; kk < ksteps && !(a.debug & 1); ++kk) {
+                const int kmax = (a.debug & 32) ? 1 : ksteps;
+                for (int kk = 0; kk < kmax && !(a.debug & 1); ++kk) {
                   umma_f16(d_tmem, make_smem_desc_rows(a_base + kk * 32, ROWB, a.boff),
                            make_smem_desc(b_base + kk * 32, ROWB), a.idesc, accum ? 1u : 0u);
                   accum = true;
@@ -487,7 +490,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       // One lane polls the barrier (32 polling lanes per warp would flood the
       // shared-memory pipe that the TMA writes go through); the others follow.
       int got = 1;
-      if (lane == 0) got = wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag);
+      if (lane == 0)
+        got = wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag, a.backoff);
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       if ((a.debug & 8) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_it < 256)
@@ -560,6 +564,14 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   });
   return fn;
+}
+
+CUtensorMapL2promotion l2promo() {
+  static const int v = getenv("CATFUSE_CONV_L2PROMO") ? atoi(getenv("CATFUSE_CONV_L2PROMO")) : 256;
+  return v == 0 ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                : (v == 64 ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
+                           : (v == 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+                                       : CU_TENSOR_MAP_L2_PROMOTION_L2_256B));
 }
 
 CUtensorMapSwizzle swizzle_for(int row_bytes) {
@@ -658,6 +670,8 @@ int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, i
   // A producer may run at most `stages` iterations ahead of the consumer
   // safely only if there are no more producers than stages.
   args.nprod = stages < kProdWarps ? stages : kProdWarps;
+  static const int env_nprod = getenv("CATFUSE_CONV_NPROD") ? atoi(getenv("CATFUSE_CONV_NPROD")) : 0;
+  if (env_nprod > 0 && env_nprod < args.nprod) args.nprod = env_nprod;
   int smem = fixed + wslab + stages * per_stage;
   // Keep every TMEM-using CTA above half the SM's shared memory so that two
   // of them can never be co-resident and contend for TMEM columns.
@@ -788,7 +802,7 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
     cuuint32_t estr[5] = {1, 1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
     CUresult r = encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(x), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(g.BK * 2),
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        l2promo(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(CF_ERR_CUDA, "tensor map (activations) failed: %d", (int)r);
   }
   {
@@ -799,7 +813,7 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
     cuuint32_t estr[2] = {1, 1};
     CUresult r = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(wp), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(g.BK * 2),
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        l2promo(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(CF_ERR_CUDA, "tensor map (weights) failed: %d", (int)r);
   }
 
@@ -834,6 +848,8 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.halo = halo;
   args.Wh = Wh;
   args.boff = env_boff;
+  static const int env_backoff = getenv("CATFUSE_CONV_BACKOFF") ? atoi(getenv("CATFUSE_CONV_BACKOFF")) : 256;
+  args.backoff = env_backoff;
   args.a_bytes = halo ? halo_bytes : 128 * g.BK * 2;
   const int grid = args.n_tiles < sm_count() ? args.n_tiles : sm_count();
 
