@@ -89,8 +89,11 @@ def main(argv=None) -> int:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--jobs", type=int, default=None)
     ap.add_argument("--ptxas-verbose", action="store_true", help="print register/smem usage")
+    ap.add_argument("--define", action="append", default=[],
+                    help="extra preprocessor definition NAME[=VALUE] (rebuild with --force)")
     args = ap.parse_args(argv)
     extra = ["-Xptxas", "-v"] if args.ptxas_verbose else []
+    extra += [f"-D{d}" for d in args.define]
     if args.ptxas_verbose:
         BUILD_DIR.mkdir(exist_ok=True)
         for src in _sources():
@@ -99,7 +102,7 @@ def main(argv=None) -> int:
             res = subprocess.run(cmd, capture_output=True, text=True)
             sys.stdout.write(res.stderr)
         return 0
-    build(force=args.force, jobs=args.jobs, verbose=True)
+    build(force=args.force, jobs=args.jobs, verbose=True, extra=extra)
     return 0
 
 

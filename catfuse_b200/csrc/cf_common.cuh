@@ -228,16 +228,6 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t row_
   return d;
 }
 
-// As make_smem_desc, but for a 128-byte-swizzled operand that may start at
-// any row of a 1024-byte-aligned swizzle pattern: the descriptor's base-offset
-// field carries the starting row within the 8-row pattern.
-__device__ __forceinline__ uint64_t make_smem_desc_rows(uint32_t saddr, uint32_t row_bytes,
-                                                        bool base_off) {
-  uint64_t d = make_smem_desc(saddr, row_bytes);
-  if (base_off && row_bytes == 128) d |= (uint64_t)((saddr >> 7) & 7u) << 49;
-  return d;
-}
-
 // Instruction descriptor: kind::f16, A/B fp16, K-major both, fp32 accum.
 __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N) {
   return (1u << 4)                          // D format: f32

@@ -47,7 +47,7 @@ __device__ int32_t g_dev_error = 0;
 // Tuning trace (CATFUSE_CONV_DEBUG bit 8): CTA 0 records clock64() stamps of
 // its first k-iterations: [0,256) producer issue, [256,512) MMA full-wait
 // done, [512,768) load-complete observed by producer-side poll (unused).
-__device__ long long g_trace[1024];
+__device__ long long g_trace[2048];
 
 namespace {
 
@@ -82,13 +82,16 @@ struct ConvArgs {
   uint32_t idesc;   // tcgen05 instruction descriptor (M=128, N=BN)
   uint32_t tmem_cols;
   int stages;
-  int debug;        // tuning experiments only: bit0 = skip MMAs, bit1 = skip epilogue math
+  int debug;        // tuning experiments only (CF_CONV_DEBUG_KNOBS=1 builds): bit0 = skip
+                    // MMAs, 1 = skip epilogue math, 4 = plain arrive for the MMA commit,
+                    // 8/128 = clock trace, 16 = no TMEM loads, 32 = one MMA per chunk,
+                    // 1024 = no TMA (plain arrive), 2048 = no weight TMA,
+                    // 4096 = epilogue only releases the accumulator
   int nprod;        // producer threads in use (<= stages)
   int wres;         // 1: the whole weight slab of the (single) N tile stays in shared memory
   int halo;         // 1: one TMA box per tile carries the whole receptive field (all taps)
   int Wh;           // halo box width (Wb + KW - 1)
   int a_bytes;      // bytes of one activation stage
-  int boff;         // set the descriptor base offset for row-shifted operands
   int backoff;      // ns of sleep between polls for the non-critical waiters
   LifParams lp;
 };
@@ -97,6 +100,9 @@ struct ConvArgs {
 #define CF_SPIN_POLL 0
 #endif
 constexpr bool kSpinPoll = CF_SPIN_POLL;
+#ifndef CF_CONV_DEBUG_KNOBS
+#define CF_CONV_DEBUG_KNOBS 0
+#endif
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int32_t site,
                                               volatile int* abort_flag, int backoff_ns = 0) {
@@ -110,13 +116,24 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
   return false;
 }
 
-// Starting point of a tile's (tap, channel chunk) walk.  A tile-dependent
-// rotation (to spread concurrent weight fetches over L2 slices) measured
-// slower than the plain order, which keeps neighbouring SMs on the same
-// weight lines; kept as a hook.
-__device__ __forceinline__ int tile_rotation(int mt, int nt, int n_all) {
-  (void)mt; (void)nt; (void)n_all;
-  return 0;
+// Warp-converged variant of wait_or_abort: all 32 lanes poll together (one
+// warp-wide try_wait) and a vote keeps the result uniform.  Role loops run on
+// whole warps with one lane issuing; a lone polling lane whose 31 siblings
+// sit in a warp-sync or block barrier ran its loop several times slower.
+__device__ __forceinline__ bool warp_wait_or_abort(uint64_t* bar, uint32_t parity, int32_t site,
+                                                   volatile int* abort_flag, int backoff_ns = 0) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    const bool done = kSpinPoll ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity);
+    if (__any_sync(0xffffffffu, done)) return true;
+    if ((i & 255u) == 255u && __any_sync(0xffffffffu, *abort_flag != 0)) return false;
+    if (backoff_ns) __nanosleep(backoff_ns);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicCAS(&g_dev_error, 0, site);
+    *abort_flag = 1;
+  }
+  __syncwarp();
+  return false;
 }
 
 __device__ __forceinline__ uint32_t tile_kmask(const ConvArgs& a, int mt) {
@@ -244,11 +261,28 @@ __device__ __forceinline__ void epi_block(const ConvArgs& a, const float* epi, i
   }
 }
 
+// Issue the KS = BK/16 MMAs of one (tap, channel chunk) back to back.  The
+// descriptors advance 32 bytes (2 in the >>4 address field) per K step; the
+// base-offset bits (address bits 7-9) are unchanged by that step.  Keeping
+// this straight-line, with the commit outside, lets the issuing thread sustain
+// one MMA per tensor-core slot; a runtime-bounded loop here issued at less
+// than half that rate.
+template <int KS>
+__device__ __forceinline__ void issue_kchunk(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t first_accum) {
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk)
+    umma_f16(d_tmem, adesc + 2ull * kk, bdesc + 2ull * kk, idesc, kk == 0 ? first_accum : 1u);
+}
+
 template <int TP, int RES, bool FAST>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_bn_lif_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const ConvArgs a) {
   constexpr int PPW = 32 / TP;  // pixels per warp
+  // Experiment switches (see ConvArgs::debug); compiled out unless the
+  // library is built with CF_CONV_DEBUG_KNOBS=1.
+  const int dbg = CF_CONV_DEBUG_KNOBS ? a.debug : 0;
   const int BN = a.BN, BK = a.BK;
   const int A_BYTES = a.a_bytes;
   const int B_BYTES = BN * BK * 2;
@@ -308,9 +342,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     // ------------------------------------------------------------ producers
     // Producer p issues the loads of global k-iterations i with i % kProdWarps
     // == p (stage i % S, phase (i / S) & 1); the MMA warp consumes in order.
-    if (lane == 0 && warp < a.nprod) {
+    if (warp < a.nprod) {
       const int p = warp;
-      if (a.wres && p == 0) {
+      if (a.wres && p == 0 && lane == 0) {
         // Load the weight slab once: block (tap, kc) at sB + (tap*n_kc + kc)*B_BYTES.
         mbar_arrive_expect_tx(w_bar, (uint32_t)(n_wblk * B_BYTES));
         for (int tap = 0; tap < a.KH * a.KW; ++tap)
@@ -318,9 +352,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tma_load_2d(sB + (size_t)(tap * a.n_kc + kc) * B_BYTES, &tmB, w_bar,
                         tap * a.Cin_p + kc * BK, 0);
       }
-      uint32_t it = 0;          // global k-iteration counter (all producers)
+      // Schedule counters advance incrementally: runtime-divisor divisions on
+      // this single-warp critical path cost more than the loads they issue.
+      int owner = 0;            // producer of the next k-iteration (it % nprod)
+      int stage = 0;            // its stage (it % S)
+      uint32_t phase = 0;       // and phase ((it / S) & 1)
       uint32_t used = 0;        // stages this producer loaded into (bit s)
       uint32_t used_phase = 0;  // phase of its latest load per stage (bit s)
+      uint32_t n_issued = 0;    // trace index
+      const int KHs = a.halo ? 1 : a.KH;  // halo: all taps in one box
+      const int KWs = a.halo ? 1 : a.KW;
       bool ok = true;
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int mt = tile / a.n_ntiles;
@@ -333,35 +374,47 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int b0 = bt * a.Bb;
         const uint32_t km = tile_kmask(a, mt);
         if (km == 0) continue;
-        const int n_tg = a.halo ? 1 : a.KH * a.KW;  // halo: all taps in one box
-        const int n_all = n_tg * a.n_kc;
-        const int rot = tile_rotation(mt, nt, n_all);
-        for (int jj = 0; jj < n_all && ok; ++jj) {
-          {
-            const int idx = (jj + rot) % n_all;
-            const int tg = idx / a.n_kc, kc = idx - tg * a.n_kc;
-            const int tap = tg;
-            const int kh = a.halo ? 0 : tap / a.KW, kw = a.halo ? 0 : tap - (tap / a.KW) * a.KW;
-            {
+        int tap = 0;
+        for (int kh = 0; kh < KHs && ok; ++kh) {
+          for (int kw = 0; kw < KWs && ok; ++kw, ++tap) {
+            for (int kc = 0; kc < a.n_kc; ++kc) {
               if (!((km >> kc) & 1u)) continue;
-              const uint32_t i = it++;
-              if ((int)(i % (uint32_t)a.nprod) != p) continue;
-              const int stage = (int)(i % (uint32_t)S);
-              const uint32_t phase = (i / (uint32_t)S) & 1u;
-              if (!wait_or_abort(&empty_bar[stage], phase ^ 1u, ERR_SITE_PRODUCER_EMPTY,
-                                 abort_flag, a.backoff)) {
+              const bool mine = owner == p;
+              const int my_stage = stage;
+              const uint32_t my_phase = phase;
+              if (++owner == a.nprod) owner = 0;
+              if (++stage == S) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              if (!mine) continue;
+              const uint32_t i = n_issued++;
+              const bool tr = blockIdx.x == 0 && i < 256 && lane == 0 && p == 0;
+              if ((dbg & 128) && tr) g_trace[512 + i] = clock64();
+              if (!warp_wait_or_abort(&empty_bar[my_stage], my_phase ^ 1u,
+                                      ERR_SITE_PRODUCER_EMPTY, abort_flag, a.backoff)) {
                 ok = false;
                 break;
               }
-              if ((a.debug & 8) && blockIdx.x == 0 && i < 256) g_trace[i] = clock64();
-              mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + STAGE_B);
-              tma_load_5d(sA + (size_t)stage * A_BYTES, &tmA, &full_bar[stage], kc * BK, a.t0,
-                          wi0 + kw, hi0 + kh, b0);
-              if (!a.wres)
-                tma_load_2d(sB + (size_t)stage * B_BYTES, &tmB, &full_bar[stage],
-                            tap * a.Cin_p + kc * BK, nt * BN);
-              used |= 1u << stage;
-              used_phase = (used_phase & ~(1u << stage)) | (phase << stage);
+              if (lane == 0) {
+                if ((dbg & 8) && tr) g_trace[i] = clock64();
+                if (dbg & 1024) {
+                  mbar_arrive(&full_bar[my_stage]);
+                } else {
+                  mbar_arrive_expect_tx(&full_bar[my_stage],
+                                        A_BYTES + ((dbg & 2048) ? 0 : STAGE_B));
+                  tma_load_5d(sA + (size_t)my_stage * A_BYTES, &tmA, &full_bar[my_stage],
+                              kc * BK, a.t0, wi0 + kw, hi0 + kh, b0);
+                  if ((dbg & 128) && tr) g_trace[1024 + i] = clock64();
+                  if (!a.wres && !(dbg & 2048))
+                    tma_load_2d(sB + (size_t)my_stage * B_BYTES, &tmB, &full_bar[my_stage],
+                                tap * a.Cin_p + kc * BK, nt * BN);
+                  if ((dbg & 128) && tr) g_trace[1280 + i] = clock64();
+                }
+              }
+              __syncwarp();
+              used |= 1u << my_stage;
+              used_phase = (used_phase & ~(1u << my_stage)) | (my_phase << my_stage);
             }
           }
         }
@@ -380,25 +433,38 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // Lane 0 issues.  tcgen05.mma queues only a few instructions ahead, so
+    // everything this thread does between two stages is a bubble in the
+    // tensor pipe unless it is shorter than the queued work: descriptors
+    // advance by adds, the schedule by compares, and the wait is one
+    // try_wait on the common path.
     if (lane == 0) {
+      const uint32_t a_step = (uint32_t)A_BYTES >> 4;  // descriptor units (16 B)
+      const uint32_t b_step = (uint32_t)B_BYTES >> 4;
+      const uint64_t a_desc0 = make_smem_desc(smem_u32(sA), ROWB);
+      const uint64_t b_desc0 = make_smem_desc(smem_u32(sB), ROWB);
+      // halo: tap (kh, kw) reads the box from row (kh*Wh + kw)*TP
+      const uint32_t row_kw = ((uint32_t)TP * ROWB) >> 4;
+      const uint32_t row_kh = ((uint32_t)(a.Wh * TP) * ROWB) >> 4;
+      const int ksteps = (dbg & 32) ? 1 : BK / 16;
+      const int n_tg = a.halo ? 1 : a.KH * a.KW;
       int stage = 0;
       uint32_t phase = 0;
+      uint64_t a_desc = a_desc0;  // descriptor of stage `stage`
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      const int ksteps = BK / 16;
       bool w_ready = false;
       int mma_it = 0;
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int mt = tile / a.n_ntiles;
         const uint32_t km = tile_kmask(a, mt);
-        const int count = __popc(km);
         if (!wait_or_abort(&tempty_bar[acc], acc_phase ^ 1u, ERR_SITE_MMA_TEMPTY, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (count == 0) {
+        if (km == 0) {
           mbar_arrive(&tfull_bar[acc]);
         } else {
           const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -409,49 +475,61 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
             w_ready = true;
           }
-          bool accum = false;
-          const int n_tg = a.halo ? 1 : a.KH * a.KW;
-          const int taps_per = a.halo ? a.KH * a.KW : 1;
-          const int n_all = n_tg * a.n_kc;
-          const int nt = tile - mt * a.n_ntiles;
-          const int rot = tile_rotation(mt, nt, n_all);
-          for (int jj = 0; jj < n_all && ok; ++jj) {
-            const int idx = (jj + rot) % n_all;
-            const int tg = idx / a.n_kc, kc = idx - tg * a.n_kc;
-            {
+          uint32_t accum = 0u;
+          uint64_t b_desc_w = b_desc0;  // weight-resident: block (tg, kc) in order
+          for (int tg = 0; tg < n_tg && ok; ++tg) {
+            for (int kc = 0; kc < a.n_kc; ++kc) {
+              if (a.wres) {
+                if (kc) b_desc_w += b_step;
+              }
               if (!((km >> kc) & 1u)) continue;
-              if (!wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag)) {
+              if (!mbar_try_wait(&full_bar[stage], phase) &&
+                  !wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag)) {
                 ok = false;
                 break;
               }
-              if ((a.debug & 8) && blockIdx.x == 0 && mma_it < 256) g_trace[256 + mma_it] = clock64();
+              if ((dbg & 8) && blockIdx.x == 0 && mma_it < 256) g_trace[256 + mma_it] = clock64();
               ++mma_it;
               // No tcgen05 fence here: the mbarrier completion already orders
-              // the TMA writes before the MMA reads, and a fence per stage
-              // would serialise consecutive MMAs.
-              const uint32_t a_stage = smem_u32(sA + (size_t)stage * A_BYTES);
-              for (int j = 0; j < taps_per; ++j) {
-                const int tap = a.halo ? j : tg;
-                // halo: the tap's operand rows start (kh*Wh + kw)*TP rows into the box
-                const uint32_t a_base =
-                    a_stage + (a.halo ? (uint32_t)(((tap / a.KW) * a.Wh + tap % a.KW) * TP) * ROWB
-                                      : 0u);
-                const uint32_t b_base =
-                    smem_u32(sB + (size_t)(a.wres ? tap * a.n_kc + kc : stage) * B_BYTES);
-                const int kmax = (a.debug & 32) ? 1 : ksteps;
-                for (int kk = 0; kk < kmax && !(a.debug & 1); ++kk) {
-                  umma_f16(d_tmem, make_smem_desc_rows(a_base + kk * 32, ROWB, a.boff),
-                           make_smem_desc(b_base + kk * 32, ROWB), a.idesc, accum ? 1u : 0u);
-                  accum = true;
+              // the TMA writes before the MMA reads.
+              if (!(dbg & 1)) {
+                if (a.halo) {
+                  // All KH*KW taps from this stage's box; weights resident,
+                  // block (tap, kc) at tap*n_kc + kc.
+                  uint64_t bd = b_desc0 + (uint64_t)((uint32_t)kc * b_step);
+                  const uint64_t bstride = (uint64_t)((uint32_t)a.n_kc * b_step);
+                  uint64_t ad_row = a_desc;
+                  for (int kh = 0; kh < a.KH; ++kh, ad_row += row_kh) {
+                    uint64_t ad = ad_row;
+                    for (int kw = 0; kw < a.KW; ++kw, ad += row_kw, bd += bstride) {
+                      if (ksteps == 4) issue_kchunk<4>(d_tmem, ad, bd, a.idesc, accum);
+                      else if (ksteps == 2) issue_kchunk<2>(d_tmem, ad, bd, a.idesc, accum);
+                      else issue_kchunk<1>(d_tmem, ad, bd, a.idesc, accum);
+                      accum = 1u;
+                    }
+                  }
+                } else {
+                  const uint64_t bd =
+                      a.wres ? b_desc_w : b_desc0 + (uint64_t)((uint32_t)stage * b_step);
+                  if (ksteps == 4) issue_kchunk<4>(d_tmem, a_desc, bd, a.idesc, accum);
+                  else if (ksteps == 2) issue_kchunk<2>(d_tmem, a_desc, bd, a.idesc, accum);
+                  else issue_kchunk<1>(d_tmem, a_desc, bd, a.idesc, accum);
+                  accum = 1u;
                 }
               }
-              if (a.debug & 4) mbar_arrive(&empty_bar[stage]);
+              if (dbg & 4) mbar_arrive(&empty_bar[stage]);
               else umma_commit(&empty_bar[stage]);
+              if ((dbg & 128) && blockIdx.x == 0 && mma_it - 1 < 256)
+                g_trace[768 + mma_it - 1] = clock64();
               if (++stage == S) {
                 stage = 0;
                 phase ^= 1u;
+                a_desc = a_desc0;
+              } else {
+                a_desc += a_step;
               }
             }
+            if (a.wres) b_desc_w += b_step;
           }
           if (!ok) break;
           umma_commit(&tfull_bar[acc]);
@@ -487,16 +565,20 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const int ht = (mt / a.n_wt) % a.n_ht;
       const int bt = mt / (a.n_wt * a.n_ht);
       const bool has_acc = tile_kmask(a, mt) != 0;
-      // One lane polls the barrier (32 polling lanes per warp would flood the
-      // shared-memory pipe that the TMA writes go through); the others follow.
-      int got = 1;
-      if (lane == 0)
-        got = wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag, a.backoff);
-      got = __shfl_sync(0xffffffffu, got, 0);
-      if (!got) break;
-      if ((a.debug & 8) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_it < 256)
+      // The whole warp waits for the accumulator (backed off, converged).
+      if (!warp_wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag,
+                              a.backoff))
+        break;
+      if ((dbg & 8) && !(dbg & 128) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_it < 256)
         g_trace[512 + ep_it] = clock64();
       tc_fence_after();
+      if (dbg & 4096) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        continue;
+      }
 
       const int wo = wt * a.Wb + wb;
       const int ho = ht * a.Hb + hb;
@@ -513,7 +595,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       }
       for (int ch = half; ch < nblk; ch += 2) {
         float r[32];
-        if (has_acc && !(a.debug & 16)) {
+        if (has_acc && !(dbg & 16)) {
           tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), r);
         } else {
 #pragma unroll
@@ -529,11 +611,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         for (int j = 0; j < 8; ++j)
           row4[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
         __syncwarp();
-        if (!(a.debug & 2))
+        if (!(dbg & 2))
           epi_block<TP, RES, FAST>(a, epi, pp, cs, pix_ok, pix, nt * BN + ch * 32 + cs * (32 / TP));
         __syncwarp();  // transpose buffer is reused by the next block
       }
-      if ((a.debug & 8) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_it < 256)
+      if ((dbg & 8) && !(dbg & 128) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_it < 256)
         g_trace[768 + ep_it] = clock64();
       ++ep_it;
       acc ^= 1;
@@ -778,7 +860,6 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   // full output row): one activation box per tile covers all taps.
   static const int env_wres = getenv("CATFUSE_CONV_WRES") ? atoi(getenv("CATFUSE_CONV_WRES")) : 1;
   static const int env_halo = getenv("CATFUSE_CONV_HALO") ? atoi(getenv("CATFUSE_CONV_HALO")) : 1;
-  static const int env_boff = getenv("CATFUSE_CONV_HALO_BOFF") ? atoi(getenv("CATFUSE_CONV_HALO_BOFF")) : 0;
   const int64_t wslab = KH * KW * g.n_kc * (int64_t)g.BN * g.BK * 2;
   const int wres = (env_wres && Cout == g.BN && wslab <= 80 * 1024) ? 1 : 0;
   const int Wh = g.Wb + (int)KW - 1;
@@ -847,7 +928,6 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.wres = wres;
   args.halo = halo;
   args.Wh = Wh;
-  args.boff = env_boff;
   static const int env_backoff = getenv("CATFUSE_CONV_BACKOFF") ? atoi(getenv("CATFUSE_CONV_BACKOFF")) : 256;
   args.backoff = env_backoff;
   args.a_bytes = halo ? halo_bytes : 128 * g.BK * 2;
@@ -889,7 +969,7 @@ int cf_check_device_error(void* stream, int32_t* code) {
 }
 
 int cf_debug_read_trace(long long* host, int n) {
-  if (!host || n <= 0 || n > 1024) return fail(CF_ERR_INVALID_ARG, "bad trace request");
+  if (!host || n <= 0 || n > 2048) return fail(CF_ERR_INVALID_ARG, "bad trace request");
   return check_cuda(cudaMemcpyFromSymbol(host, g_trace, n * sizeof(long long)), "read trace");
 }
 
