@@ -228,6 +228,13 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t row_
   return d;
 }
 
+// Global nanosecond timer (tuning traces).
+__device__ __forceinline__ long long globaltimer_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Instruction descriptor: kind::f16, A/B fp16, K-major both, fp32 accum.
 __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N) {
   return (1u << 4)                          // D format: f32

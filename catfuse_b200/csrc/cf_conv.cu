@@ -58,6 +58,10 @@ constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter
 constexpr int kConvThreads = 32 * (kProdWarps + 1 + kEpiWarps);
 constexpr int kEpiRowStride = 36;  // floats per transpose row (bank-conflict free)
 constexpr int kEpiBytes = kEpiWarps * 32 * kEpiRowStride * 4;
+// Channel-major kernel: three epilogue warps per TMEM lane quarter (its
+// epilogue is latency-bound; more resident warps hide the latency).
+constexpr int kTEpiWarps = 12;
+constexpr int kTThreads = 32 * (kProdWarps + 1 + kTEpiWarps);
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kMaxTP = 8;  // time steps per launch; longer T runs in blocks of 8
 
@@ -93,6 +97,9 @@ struct ConvArgs {
   int Wh;           // halo box width (Wb + KW - 1)
   int a_bytes;      // bytes of one activation stage
   int backoff;      // ns of sleep between polls for the non-critical waiters
+  int tmode;        // 1: channel-major kernel (conv_t_kernel)
+  int NR;           // channel-major kernel: pixel x time rows per tile (MMA N)
+  int lwb, lhb;     // log2 of Wb and Hb
   LifParams lp;
 };
 
@@ -631,6 +638,403 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
 }
 
+
+// --------------------------------------------------------------------------
+// Channel-major variant (Cout % 128 == 0).  The GEMM roles swap: D[co][row] =
+// sum_k W[co][k] X[row][k] with M = 128 output channels (operand A = weight
+// tile) and N = NR (256 or 128) pixel x time rows (operand B = activation
+// tile).  An M=128, N=256 MMA carries 128 tensor-core cycles of work per
+// instruction, twice the N=128 case, so the issuing thread's per-stage
+// bookkeeping (barrier wait, commit) hides behind the queued MMAs instead of
+// stalling the pipe.  The accumulator lane is the output channel: each
+// epilogue thread owns one channel and runs the LIF recurrence of 32/TP
+// pixels over TP steps straight from its tcgen05.ld registers, with the BN
+// affine as two per-thread scalars and no shared-memory transpose.
+// Warp roles and the producer/MMA pipeline are those of conv_bn_lif_kernel.
+// --------------------------------------------------------------------------
+constexpr int kStageRowB = 80;  // bytes per staging row: 32 halves + pad (16-B aligned)
+constexpr int kStageBytes = 32 * kStageRowB;
+
+// Epilogue of one 32-column chunk of the channel-major accumulator.  Lane =
+// output channel co; r[pp*TP + t] = z of pixel p0+pp, step t.  The LIF runs
+// in these registers; the fp16 results go through the warp's staging rows
+// (row = pixel-time column, 32 channels) so that each lane then writes one
+// (pixel, step) row of 32 channels as four 16-byte stores.  Identity spikes
+// come in the same way in reverse.
+template <int TP, int RES, bool FAST, bool FULLT>
+__device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[32], int co,
+                                            int co_base, float sc, float sh, int wt, int ht,
+                                            int bt, int p0, uint8_t* stage, int lane,
+                                            long long* tr = nullptr) {
+  constexpr int PP = 32 / TP;  // pixels in this chunk
+  constexpr bool kIdent = (RES != CF_RES_NONE && RES != CF_RES_Z_ONLY);
+  constexpr bool kLif = (RES != CF_RES_Z_ONLY);
+  constexpr bool full_t = FULLT;  // all TP steps valid: straight-line recurrences
+  // Row of this lane in the transposed phase: pixel rp, step rt.
+  const int rp = lane / TP, rt = lane - (lane / TP) * TP;
+  int64_t rpix;
+  bool rok;
+  {
+    const int p = p0 + rp;
+    const int wo = (wt << a.lwb) + (p & ((1 << a.lwb) - 1));
+    const int ho = (ht << a.lhb) + ((p >> a.lwb) & ((1 << a.lhb) - 1));
+    const int b = bt * a.Bb + (p >> (a.lwb + a.lhb));
+    rok = wo < a.Wo && ho < a.Ho && b < a.B && rt < a.tcount;
+    rpix = ((int64_t)b * a.Ho + ho) * a.Wo + wo;
+  }
+  const int64_t row_off = (rpix * a.T + a.t0 + rt) * a.Cout + co_base;
+  uint4* srow = reinterpret_cast<uint4*>(stage + lane * kStageRowB);
+  const __half* scol = reinterpret_cast<const __half*>(stage) + lane;  // + row * 40
+
+  float idv[kIdent ? 32 : 1];
+  if constexpr (kIdent) {
+    uint4 q4[4] = {};
+    if (rok) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.identity + row_off);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) q4[k] = src[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) srow[k] = q4[k];
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) idv[j] = __half2float(scol[j * (kStageRowB / 2)]);
+    __syncwarp();
+  }
+
+  // Membranes of this lane's channel for the chunk's pixels (coalesced over
+  // the warp's 32 channels), all issued before any store.
+  int64_t pix[PP];
+  bool ok[PP];
+  float v[PP];
+  if ((1 << a.lwb) >= PP) {
+    // The chunk's pixels are consecutive in one output row.
+    const int wo0 = (wt << a.lwb) + (p0 & ((1 << a.lwb) - 1));
+    const int ho = (ht << a.lhb) + ((p0 >> a.lwb) & ((1 << a.lhb) - 1));
+    const int b = bt * a.Bb + (p0 >> (a.lwb + a.lhb));
+    const bool row_ok = ho < a.Ho && b < a.B;
+    const int64_t pix0 = ((int64_t)b * a.Ho + ho) * a.Wo + wo0;
+#pragma unroll
+    for (int pp = 0; pp < PP; ++pp) {
+      ok[pp] = row_ok && wo0 + pp < a.Wo;
+      pix[pp] = pix0 + pp;
+    }
+  } else {
+#pragma unroll
+    for (int pp = 0; pp < PP; ++pp) {
+      const int p = p0 + pp;
+      const int wo = (wt << a.lwb) + (p & ((1 << a.lwb) - 1));
+      const int ho = (ht << a.lhb) + ((p >> a.lwb) & ((1 << a.lhb) - 1));
+      const int b = bt * a.Bb + (p >> (a.lwb + a.lhb));
+      ok[pp] = wo < a.Wo && ho < a.Ho && b < a.B;
+      pix[pp] = ((int64_t)b * a.Ho + ho) * a.Wo + wo;
+    }
+  }
+  if constexpr (kLif) {
+#pragma unroll
+    for (int pp = 0; pp < PP; ++pp) v[pp] = (a.v_in && ok[pp]) ? a.v_in[pix[pp] * a.Cout + co] : 0.f;
+  }
+
+  __half* hrow = reinterpret_cast<__half*>(stage) + lane;
+  if (tr) tr[0] = clock64();
+#pragma unroll
+  for (int pp = 0; pp < PP; ++pp) {
+    float vv = kLif ? v[pp] : 0.f;
+#pragma unroll
+    for (int t = 0; t < TP; ++t) {
+      const int j = pp * TP + t;
+      if (full_t || t < a.tcount) {
+        float z = fmaf(r[j], sc, sh);
+        float o;
+        if constexpr (RES == CF_RES_ADD_PRE) z = __fadd_rn(z, idv[j]);
+        if constexpr (!kLif) {
+          o = z;
+        } else {
+          o = lif_any<FAST>(vv, z, a.lp);
+          if constexpr (RES == CF_RES_ADD_POST) o += idv[j];
+          else if constexpr (RES == CF_RES_AND_POST) o *= idv[j];
+          else if constexpr (RES == CF_RES_IAND_POST) o = idv[j] * (1.f - o);
+        }
+        hrow[j * (kStageRowB / 2)] = __float2half_rn(o);
+      }
+    }
+    if (kLif) v[pp] = vv;
+  }
+  if constexpr (kLif) {
+    if (a.v_out) {
+#pragma unroll
+      for (int pp = 0; pp < PP; ++pp)
+        if (ok[pp]) a.v_out[pix[pp] * a.Cout + co] = v[pp];
+    }
+  }
+  if (tr) tr[1] = clock64();
+  __syncwarp();
+  if (rok) {
+    uint4* dst = reinterpret_cast<uint4*>(a.out + row_off);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dst[k] = srow[k];
+  }
+  __syncwarp();  // the staging rows are reused by the next chunk
+  if (tr) tr[2] = clock64();
+}
+
+template <int TP, int RES, bool FAST>
+__global__ void __launch_bounds__(kTThreads, 1)
+    conv_t_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                  const ConvArgs a) {
+  const int dbg = CF_CONV_DEBUG_KNOBS ? a.debug : 0;  // see ConvArgs::debug
+  const int BK = a.BK;
+  const int NR = a.NR;
+  const int X_BYTES = NR * BK * 2;   // activation tile of one stage
+  const int W_BYTES = 128 * BK * 2;  // weight tile of one stage
+  const uint32_t ROWB = (uint32_t)BK * 2;
+  const int S = a.stages;
+  const int n_ct = a.n_ntiles;       // output-channel tiles of 128
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sX = smem;
+  uint8_t* sW = sX + (size_t)S * X_BYTES;
+  uint8_t* sStage = sW + (size_t)S * W_BYTES;  // epilogue staging, kStageBytes per warp
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStage + kTEpiWarps * kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if ((dbg & 8) && threadIdx.x == 0 && blockIdx.x < 256) g_trace[blockIdx.x * 4] = globaltimer_ns();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], kTEpiWarps);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp < kProdWarps && lane == 0) {
+    prefetch_tmap(&tmX);
+    prefetch_tmap(&tmW);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if ((dbg & 8) && threadIdx.x == 0 && blockIdx.x < 256) g_trace[blockIdx.x * 4 + 1] = globaltimer_ns();
+
+  if (warp < kProdWarps) {
+    // ------------------------------------------------------------ producers
+    if (warp < a.nprod) {
+      const int p = warp;
+      int owner = 0, stage = 0;
+      uint32_t phase = 0;
+      uint32_t used = 0, used_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
+        const int pt = tile / n_ct;
+        const int ct = tile - pt * n_ct;
+        const int wt = pt % a.n_wt;
+        const int ht = (pt / a.n_wt) % a.n_ht;
+        const int bt = pt / (a.n_wt * a.n_ht);
+        const int wi0 = wt * a.Wb * a.stride - a.pad;
+        const int hi0 = ht * a.Hb * a.stride - a.pad;
+        const int b0 = bt * a.Bb;
+        const uint32_t km = tile_kmask(a, pt);
+        if (km == 0) continue;
+        int tap = 0;
+        for (int kh = 0; kh < a.KH && ok; ++kh) {
+          for (int kw = 0; kw < a.KW && ok; ++kw, ++tap) {
+            for (int kc = 0; kc < a.n_kc; ++kc) {
+              if (!((km >> kc) & 1u)) continue;
+              const bool mine = owner == p;
+              const int my_stage = stage;
+              const uint32_t my_phase = phase;
+              if (++owner == a.nprod) owner = 0;
+              if (++stage == S) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              if (!mine) continue;
+              if (!warp_wait_or_abort(&empty_bar[my_stage], my_phase ^ 1u,
+                                      ERR_SITE_PRODUCER_EMPTY, abort_flag, a.backoff)) {
+                ok = false;
+                break;
+              }
+              if (lane == 0 && (dbg & 1024)) {
+                mbar_arrive(&full_bar[my_stage]);
+              } else if (lane == 0) {
+                mbar_arrive_expect_tx(&full_bar[my_stage], X_BYTES + W_BYTES);
+                tma_load_5d(sX + (size_t)my_stage * X_BYTES, &tmX, &full_bar[my_stage],
+                            kc * BK, a.t0, wi0 + kw, hi0 + kh, b0);
+                tma_load_2d(sW + (size_t)my_stage * W_BYTES, &tmW, &full_bar[my_stage],
+                            tap * a.Cin_p + kc * BK, ct * 128);
+              }
+              __syncwarp();
+              used |= 1u << my_stage;
+              used_phase = (used_phase & ~(1u << my_stage)) | (my_phase << my_stage);
+            }
+          }
+        }
+      }
+      if (!ok) {
+        for (int st = 0; st < S; ++st) {
+          if (!((used >> st) & 1u)) continue;
+          for (uint32_t q = 0; q < (1u << 16); ++q)
+            if (mbar_try_wait(&full_bar[st], (used_phase >> st) & 1u)) break;
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t x_step = (uint32_t)X_BYTES >> 4;
+      const uint32_t w_step = (uint32_t)W_BYTES >> 4;
+      const uint64_t x_desc0 = make_smem_desc(smem_u32(sX), ROWB);
+      const uint64_t w_desc0 = make_smem_desc(smem_u32(sW), ROWB);
+      const int ksteps = BK / 16;
+      const int n_tap = a.KH * a.KW;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint64_t xd = x_desc0, wd = w_desc0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
+        const int pt = tile / n_ct;
+        const uint32_t km = tile_kmask(a, pt);
+        if (!wait_or_abort(&tempty_bar[acc], acc_phase ^ 1u, ERR_SITE_MMA_TEMPTY, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (km == 0) {
+          mbar_arrive(&tfull_bar[acc]);
+        } else {
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * NR);
+          uint32_t accum = 0u;
+          for (int tg = 0; tg < n_tap && ok; ++tg) {
+            for (int kc = 0; kc < a.n_kc; ++kc) {
+              if (!((km >> kc) & 1u)) continue;
+              if (!mbar_try_wait(&full_bar[stage], phase) &&
+                  !wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag)) {
+                ok = false;
+                break;
+              }
+              if (dbg & 1) {
+              } else if (ksteps == 4) issue_kchunk<4>(d_tmem, wd, xd, a.idesc, accum);
+              else if (ksteps == 2) issue_kchunk<2>(d_tmem, wd, xd, a.idesc, accum);
+              else issue_kchunk<1>(d_tmem, wd, xd, a.idesc, accum);
+              accum = 1u;
+              umma_commit(&empty_bar[stage]);
+              if (++stage == S) {
+                stage = 0;
+                phase ^= 1u;
+                xd = x_desc0;
+                wd = w_desc0;
+              } else {
+                xd += x_step;
+                wd += w_step;
+              }
+            }
+          }
+          if (!ok) break;
+          umma_commit(&tfull_bar[acc]);
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      umma_commit(done_bar);
+      for (uint32_t p = 0; p < kMaxPolls; ++p)
+        if (mbar_try_wait(done_bar, 0)) break;
+      if ((dbg & 8) && blockIdx.x < 256) g_trace[blockIdx.x * 4 + 2] = globaltimer_ns();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Warp e reads TMEM lane quarter q = warp % 4 (channels q*32 + lane of the
+    // tile) and the 32-column chunks k, k+3, ... with k = e / 4.
+    const int e = warp - kEpiWarp0;
+    const int q = warp & 3;
+    const int k = e >> 2;
+    const int n_chunk = NR >> 5;
+    int last_chunk = k;
+    while (last_chunk + 3 < n_chunk) last_chunk += 3;
+    uint8_t* stage = sStage + e * kStageBytes;
+    int ep_n = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+      const int pt = tile / n_ct;
+      const int ct = tile - pt * n_ct;
+      const int wt = pt % a.n_wt;
+      const int ht = (pt / a.n_wt) % a.n_ht;
+      const int bt = pt / (a.n_wt * a.n_ht);
+      const bool has_acc = tile_kmask(a, pt) != 0;
+      const int co = ct * 128 + q * 32 + lane;
+      const float sc = a.scale ? __ldg(a.scale + co) : 1.f;
+      const float sh = a.shift ? __ldg(a.shift + co) : 0.f;
+      if (!warp_wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag,
+                              a.backoff))
+        break;
+      tc_fence_after();
+      const bool tr = (dbg & 16) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_n < 8;
+      if (tr) g_trace[1024 + ep_n * 16] = clock64();
+      for (int ch = k; ch < n_chunk; ch += 3) {
+        const int col = ch * 32;
+        const int c0 = (ch / 3) * 32;  // trace slot
+        float r[32];
+        if (has_acc) {
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * NR + col), r);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0.f;
+        }
+        if (tr) g_trace[1024 + ep_n * 16 + 1 + (c0 / 32) * 2] = clock64();
+        if (ch == last_chunk) {
+          // Last read of this warp: hand the accumulator back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        }
+        if (dbg & 2) {
+        } else if (a.tcount == TP) {
+          epi_chunk_t<TP, RES, FAST, true>(a, r, co, ct * 128 + q * 32, sc, sh, wt, ht, bt,
+                                           col / TP, stage, lane,
+                                           tr ? &g_trace[1200 + ep_n * 16 + (c0 / 32) * 3] : nullptr);
+        } else {
+          epi_chunk_t<TP, RES, FAST, false>(a, r, co, ct * 128 + q * 32, sc, sh, wt, ht, bt,
+                                            col / TP, stage, lane);
+        }
+        if (tr) g_trace[1024 + ep_n * 16 + 2 + (c0 / 32) * 2] = clock64();
+      }
+      ++ep_n;
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+  if ((dbg & 8) && threadIdx.x == 0 && blockIdx.x < 256) g_trace[blockIdx.x * 4 + 3] = globaltimer_ns();
+}
+
 // --------------------------------------------------------------------------
 // host side
 // --------------------------------------------------------------------------
@@ -669,7 +1073,16 @@ int next_pow2(int v) {
 
 struct Geometry {
   int TP, Wb, Hb, Bb, n_wt, n_ht, n_bt, n_mtiles, BN, BK, n_kc;
+  int tmode;  // 1: channel-major kernel (conv_t_kernel), M = 128 channels, N = NR rows
+  int NR;
 };
+
+// The channel-major kernel serves every layer whose output channels come in
+// whole 128-channel tiles.
+bool use_tmode(int64_t Cout) {
+  static const int env = getenv("CATFUSE_CONV_TMODE") ? atoi(getenv("CATFUSE_CONV_TMODE")) : 1;
+  return env != 0 && Cout % 128 == 0;
+}
 
 // Choose the pixel box (Wb x Hb x Bb = 128/TP, powers of two) that wastes the
 // fewest padded output pixels; ties go to the wider box (longer contiguous
@@ -729,10 +1142,24 @@ int make_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout, in
                   int64_t stride, bool sparse, Geometry& g) {
   const int tc = (int)(T < kMaxTP ? T : kMaxTP);
   g.TP = next_pow2(tc);
-  choose_box(128 / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
-  g.BN = choose_bn((int)Cout, g.n_mtiles);
   g.BK = choose_bk((int)Cin_p, sparse);
   g.n_kc = (int)(Cin_p / g.BK);
+  if (use_tmode(Cout)) {
+    // N = 256 rows per tile unless that leaves a quarter of the SMs idle.
+    g.tmode = 1;
+    g.BN = 128;
+    g.NR = 256;
+    choose_box(g.NR / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
+    if ((long)g.n_mtiles * (Cout / 128) < (148 * 3) / 4) {
+      g.NR = 128;
+      choose_box(g.NR / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
+    }
+    return CF_OK;
+  }
+  g.tmode = 0;
+  g.NR = 128;
+  choose_box(128 / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
+  g.BN = choose_bn((int)Cout, g.n_mtiles);
   return g.BN ? CF_OK : fail(CF_ERR_UNSUPPORTED, "Cout=%lld must be a multiple of 32", (long long)Cout);
 }
 
@@ -769,11 +1196,42 @@ int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, i
   return check_launch("conv_bn_lif launch");
 }
 
+template <int TP, int RES, bool FAST>
+int launch_t(const CUtensorMap& tmX, const CUtensorMap& tmW, ConvArgs args, int grid,
+             cudaStream_t stream) {
+  const int per_stage = (args.NR + 128) * args.BK * 2;
+  const int fixed = 1024 + kTEpiWarps * kStageBytes + 256;
+  int stages = (kSmemBudget - fixed) / per_stage;
+  if (stages > 8) stages = 8;
+  if (args.stages > 1 && args.stages < stages) stages = args.stages;  // tuning override
+  if (stages < 2) return fail(CF_ERR_UNSUPPORTED, "conv tile does not fit shared memory");
+  args.stages = stages;
+  args.nprod = stages < kProdWarps ? stages : kProdWarps;
+  int smem = fixed + stages * per_stage;
+  if (smem < 120 * 1024) smem = 120 * 1024;  // one TMEM-owning CTA per SM
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(conv_t_kernel<TP, RES, FAST>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(conv_t)");
+    attr_set = true;
+  }
+  conv_t_kernel<TP, RES, FAST><<<grid, kTThreads, smem, stream>>>(tmX, tmW, args);
+  return check_launch("conv_t launch");
+}
+
+template <int TP, int RES, bool FAST>
+int launch_any(const CUtensorMap& A, const CUtensorMap& W, const ConvArgs& args, int grid,
+               cudaStream_t s) {
+  return args.tmode ? launch_t<TP, RES, FAST>(A, W, args, grid, s)
+                    : launch_inst<TP, RES, FAST>(A, W, args, grid, s);
+}
+
 template <int TP, int RES>
 int dispatch_fast(bool fast, const CUtensorMap& A, const CUtensorMap& W, const ConvArgs& args,
                   int grid, cudaStream_t s) {
-  return fast ? launch_inst<TP, RES, true>(A, W, args, grid, s)
-              : launch_inst<TP, RES, false>(A, W, args, grid, s);
+  return fast ? launch_any<TP, RES, true>(A, W, args, grid, s)
+              : launch_any<TP, RES, false>(A, W, args, grid, s);
 }
 
 template <int TP>
@@ -785,7 +1243,7 @@ int dispatch_res(int res, bool fast, const CUtensorMap& A, const CUtensorMap& W,
     case CF_RES_AND_POST: return dispatch_fast<TP, CF_RES_AND_POST>(fast, A, W, args, grid, s);
     case CF_RES_IAND_POST: return dispatch_fast<TP, CF_RES_IAND_POST>(fast, A, W, args, grid, s);
     case CF_RES_ADD_PRE: return dispatch_fast<TP, CF_RES_ADD_PRE>(fast, A, W, args, grid, s);
-    default: return launch_inst<TP, CF_RES_Z_ONLY, true>(A, W, args, grid, s);
+    default: return launch_any<TP, CF_RES_Z_ONLY, true>(A, W, args, grid, s);
   }
 }
 
@@ -861,11 +1319,11 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   static const int env_wres = getenv("CATFUSE_CONV_WRES") ? atoi(getenv("CATFUSE_CONV_WRES")) : 1;
   static const int env_halo = getenv("CATFUSE_CONV_HALO") ? atoi(getenv("CATFUSE_CONV_HALO")) : 1;
   const int64_t wslab = KH * KW * g.n_kc * (int64_t)g.BN * g.BK * 2;
-  const int wres = (env_wres && Cout == g.BN && wslab <= 80 * 1024) ? 1 : 0;
+  const int wres = (!g.tmode && env_wres && Cout == g.BN && wslab <= 80 * 1024) ? 1 : 0;
   const int Wh = g.Wb + (int)KW - 1;
   const int halo_bytes = ((g.TP * Wh * (int)KH * g.BK * 2) + 1023) / 1024 * 1024;
   const int fixed_bytes = 1024 + kEpiBytes + 256;
-  const int halo = (env_halo && wres && stride == 1 && g.Hb == 1 && g.Bb == 1 &&
+  const int halo = (!g.tmode && env_halo && wres && stride == 1 && g.Hb == 1 && g.Bb == 1 &&
                     g.Wb * g.TP == 128 && g.TP >= 4 && g.BK == 64 && Wh <= 256 && KH <= 256 &&
                     fixed_bytes + wslab + 2 * halo_bytes <= kSmemBudget) ? 1 : 0;
   CUtensorMap tmA, tmB;
@@ -890,7 +1348,7 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
     const int64_t K = KH * KW * Cin_p;
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)Cout};
     cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)g.BK, (cuuint32_t)g.BN};
+    cuuint32_t box[2] = {(cuuint32_t)g.BK, (cuuint32_t)g.BN};  // channel-major: BN = 128 = M
     cuuint32_t estr[2] = {1, 1};
     CUresult r = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(wp), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(g.BK * 2),
@@ -916,8 +1374,17 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.kc_all = g.n_kc >= 32 ? 0xFFFFFFFFu : ((1u << g.n_kc) - 1u);
   args.BN = g.BN;
   args.BK = g.BK;
-  args.idesc = make_idesc_f16(128, g.BN);
-  args.tmem_cols = (uint32_t)(2 * g.BN < 32 ? 32 : 2 * g.BN);
+  args.tmode = g.tmode;
+  args.NR = g.NR;
+  args.lwb = __builtin_ctz((unsigned)g.Wb);
+  args.lhb = __builtin_ctz((unsigned)g.Hb);
+  if (g.tmode) {
+    args.idesc = make_idesc_f16(128, g.NR);
+    args.tmem_cols = (uint32_t)(2 * g.NR);
+  } else {
+    args.idesc = make_idesc_f16(128, g.BN);
+    args.tmem_cols = (uint32_t)(2 * g.BN < 32 ? 32 : 2 * g.BN);
+  }
   args.lp = make_lif(tau, v_th, v_reset, hard_reset, decay_input);
   const bool fast = args.lp.decay_input && args.lp.hard_reset && args.lp.tau_pow2;
   // Tuning overrides for experiments: CATFUSE_CONV_STAGES, CATFUSE_CONV_DEBUG.

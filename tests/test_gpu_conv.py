@@ -58,6 +58,13 @@ SHAPES = [
     (4, 2, 64, 64, 32, 32, 3, 1, 1),
     (2, 2, 64, 64, 64, 64, 3, 1, 1),
     (4, 3, 64, 32, 32, 32, 3, 1, 1),
+    # channel-major kernel (Cout % 128 == 0): N = 256 / 128 pixel-time rows,
+    # ragged pixel tiles, T = 1 / 3 / chunked T, several channel tiles
+    (12, 1, 32, 128, 5, 5, 3, 1, 1),
+    (2, 3, 48, 128, 10, 6, 3, 1, 1),
+    (1, 2, 32, 256, 7, 9, 3, 1, 1),
+    (3, 1, 64, 384, 9, 9, 3, 2, 1),
+    (4, 8, 128, 128, 32, 32, 3, 1, 1),
 ]
 
 
@@ -81,10 +88,11 @@ def test_conv_bn_lif_vs_oracle(dev, shape):
     assert s.mean() > 0.005, "degenerate case: almost no spikes"
 
 
+@pytest.mark.parametrize("C", [64, 128])
 @pytest.mark.parametrize("mode", ["add", "add_pre", "and", "iand"])
-def test_conv_residual_modes(dev, mode):
+def test_conv_residual_modes(dev, mode, C):
     ops = _ops()
-    T, B, C, H, W = 4, 2, 64, 8, 8
+    T, B, H, W = 4, 2, 8, 8
     x, w, scale, shift = _case(T, B, C, C, H, W, 3, seed=11)
     g = torch.Generator().manual_seed(12)
     ident = (torch.rand(T, B, C, H, W, generator=g) < 0.3).float() * (1 + (torch.rand(T, B, C, H, W, generator=g) < 0.3).float())
@@ -98,11 +106,12 @@ def test_conv_residual_modes(dev, mode):
     assert np.abs(v - v_o)[ok].max() <= 1e-4
 
 
-def test_conv_state_carry_and_inplace(dev):
+@pytest.mark.parametrize("C", [32, 128])
+def test_conv_state_carry_and_inplace(dev, C):
     """v_in -> v_out StateCarry; v_in may alias v_out; T-chunked launch equals
     the oracle with v carried."""
     ops = _ops()
-    T, B, C, H, W = 10, 2, 32, 6, 6
+    T, B, H, W = 10, 2, 6, 6
     x, w, scale, shift = _case(T, B, C, C, H, W, 3, seed=21)
     g = torch.Generator().manual_seed(22)
     v0 = torch.randn(B, C, H, W, generator=g) * 0.5
