@@ -61,6 +61,7 @@ constexpr int kEpiBytes = kEpiWarps * 32 * kEpiRowStride * 4;
 // Channel-major kernel: three epilogue warps per TMEM lane quarter (its
 // epilogue is latency-bound; more resident warps hide the latency).
 constexpr int kTEpiWarps = 12;
+constexpr int kTSmemBudget = 227 * 1024;  // the whole opt-in shared memory of a CTA
 constexpr int kTThreads = 32 * (kProdWarps + 1 + kTEpiWarps);
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kMaxTP = 8;  // time steps per launch; longer T runs in blocks of 8
@@ -98,6 +99,8 @@ struct ConvArgs {
   int a_bytes;      // bytes of one activation stage
   int backoff;      // ns of sleep between polls for the non-critical waiters
   int tmode;        // 1: channel-major kernel (conv_t_kernel)
+  int khbox;        // channel-major: one activation box covers all kh taps of a kw column
+  int wstages;      // channel-major: weight ring depth (act ring depth = stages)
   int NR;           // channel-major kernel: pixel x time rows per tile (MMA N)
   int lwb, lhb;     // log2 of Wb and Hb
   LifParams lp;
@@ -785,21 +788,30 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const int dbg = CF_CONV_DEBUG_KNOBS ? a.debug : 0;  // see ConvArgs::debug
   const int BK = a.BK;
   const int NR = a.NR;
-  const int X_BYTES = NR * BK * 2;   // activation tile of one stage
-  const int W_BYTES = 128 * BK * 2;  // weight tile of one stage
+  const int XA = a.a_bytes;          // activation box of one act stage
+  const int W_BYTES = 128 * BK * 2;  // weight tile of one weight stage
   const uint32_t ROWB = (uint32_t)BK * 2;
-  const int S = a.stages;
+  const int SA = a.stages;           // activation stages
+  const int SW = a.wstages;          // weight stages
   const int n_ct = a.n_ntiles;       // output-channel tiles of 128
+  // Act steps walk (gh, gw, kc); each serves nsub weight sub-steps.  In the
+  // kh-box mode (stride 1, tile inside one image) one activation box of
+  // Hb+KH-1 rows covers all kh taps of a kw column: tap (kh, kw) reads it
+  // from row kh*Wb*TP on, and the act step loop has gh = 0 only.
+  const int n_gh = a.khbox ? 1 : a.KH;
+  const int nsub = a.khbox ? a.KH : 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = smem;
-  uint8_t* sW = sX + (size_t)S * X_BYTES;
-  uint8_t* sStage = sW + (size_t)S * W_BYTES;  // epilogue staging, kStageBytes per warp
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStage + kTEpiWarps * kStageBytes);
-  uint64_t* empty_bar = full_bar + S;
-  uint64_t* tfull_bar = empty_bar + S;
+  uint8_t* sW = sX + (size_t)SA * XA;
+  uint8_t* sStage = sW + (size_t)SW * W_BYTES;  // epilogue staging, kStageBytes per warp
+  uint64_t* afull_bar = reinterpret_cast<uint64_t*>(sStage + kTEpiWarps * kStageBytes);
+  uint64_t* aempty_bar = afull_bar + SA;
+  uint64_t* wfull_bar = aempty_bar + SA;
+  uint64_t* wempty_bar = wfull_bar + SW;
+  uint64_t* tfull_bar = wempty_bar + SW;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* done_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -810,9 +822,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
   if ((dbg & 8) && threadIdx.x == 0 && blockIdx.x < 256) g_trace[blockIdx.x * 4] = globaltimer_ns();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&afull_bar[s], 1);
+      mbar_init(&aempty_bar[s], 1);
+    }
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&wfull_bar[s], 1);
+      mbar_init(&wempty_bar[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
@@ -836,8 +852,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   if ((dbg & 8) && threadIdx.x == 0 && blockIdx.x < 256) g_trace[blockIdx.x * 4 + 1] = globaltimer_ns();
 
-  if (warp < kProdWarps) {
-    // ------------------------------------------------------------ producers
+  if (!a.khbox && warp < kProdWarps) {
+    // ---------------------------------------------- paired producers (warps 0-3)
+    // Stage s of both rings carries one (tap, chunk): activation tile and
+    // weight tile on afull[s]; producer p issues k-iterations i % nprod == p.
     if (warp < a.nprod) {
       const int p = warp;
       int owner = 0, stage = 0;
@@ -864,24 +882,26 @@ __global__ void __launch_bounds__(kTThreads, 1)
               const int my_stage = stage;
               const uint32_t my_phase = phase;
               if (++owner == a.nprod) owner = 0;
-              if (++stage == S) {
+              if (++stage == SA) {
                 stage = 0;
                 phase ^= 1u;
               }
               if (!mine) continue;
-              if (!warp_wait_or_abort(&empty_bar[my_stage], my_phase ^ 1u,
+              if (!warp_wait_or_abort(&aempty_bar[my_stage], my_phase ^ 1u,
                                       ERR_SITE_PRODUCER_EMPTY, abort_flag, a.backoff)) {
                 ok = false;
                 break;
               }
-              if (lane == 0 && (dbg & 1024)) {
-                mbar_arrive(&full_bar[my_stage]);
-              } else if (lane == 0) {
-                mbar_arrive_expect_tx(&full_bar[my_stage], X_BYTES + W_BYTES);
-                tma_load_5d(sX + (size_t)my_stage * X_BYTES, &tmX, &full_bar[my_stage],
-                            kc * BK, a.t0, wi0 + kw, hi0 + kh, b0);
-                tma_load_2d(sW + (size_t)my_stage * W_BYTES, &tmW, &full_bar[my_stage],
-                            tap * a.Cin_p + kc * BK, ct * 128);
+              if (lane == 0) {
+                if (dbg & 1024) {
+                  mbar_arrive(&afull_bar[my_stage]);
+                } else {
+                  mbar_arrive_expect_tx(&afull_bar[my_stage], XA + W_BYTES);
+                  tma_load_5d(sX + (size_t)my_stage * XA, &tmX, &afull_bar[my_stage], kc * BK,
+                              a.t0, wi0 + kw, hi0 + kh, b0);
+                  tma_load_2d(sW + (size_t)my_stage * W_BYTES, &tmW, &afull_bar[my_stage],
+                              tap * a.Cin_p + kc * BK, ct * 128);
+                }
               }
               __syncwarp();
               used |= 1u << my_stage;
@@ -891,63 +911,208 @@ __global__ void __launch_bounds__(kTThreads, 1)
         }
       }
       if (!ok) {
-        for (int st = 0; st < S; ++st) {
+        for (int st = 0; st < SA; ++st) {
           if (!((used >> st) & 1u)) continue;
           for (uint32_t q = 0; q < (1u << 16); ++q)
-            if (mbar_try_wait(&full_bar[st], (used_phase >> st) & 1u)) break;
+            if (mbar_try_wait(&afull_bar[st], (used_phase >> st) & 1u)) break;
+        }
+      }
+    }
+  } else if (warp == 0) {
+    // ------------------------------------------------- activation producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used = 0, used_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
+      const int pt = tile / n_ct;
+      const int wt = pt % a.n_wt;
+      const int ht = (pt / a.n_wt) % a.n_ht;
+      const int bt = pt / (a.n_wt * a.n_ht);
+      const int wi0 = wt * a.Wb * a.stride - a.pad;
+      const int hi0 = ht * a.Hb * a.stride - a.pad;
+      const int b0 = bt * a.Bb;
+      const uint32_t km = tile_kmask(a, pt);
+      if (km == 0) continue;
+      for (int gh = 0; gh < n_gh && ok; ++gh) {
+        for (int gw = 0; gw < a.KW && ok; ++gw) {
+          for (int kc = 0; kc < a.n_kc; ++kc) {
+            if (!((km >> kc) & 1u)) continue;
+            if (!warp_wait_or_abort(&aempty_bar[stage], phase ^ 1u, ERR_SITE_PRODUCER_EMPTY,
+                                    abort_flag, a.backoff)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              if (dbg & 1024) {
+                mbar_arrive(&afull_bar[stage]);
+              } else {
+                mbar_arrive_expect_tx(&afull_bar[stage], XA);
+                tma_load_5d(sX + (size_t)stage * XA, &tmX, &afull_bar[stage], kc * BK, a.t0,
+                            wi0 + gw, hi0 + gh, b0);
+              }
+            }
+            __syncwarp();
+            used |= 1u << stage;
+            used_phase = (used_phase & ~(1u << stage)) | (phase << stage);
+            if (++stage == SA) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+    }
+    if (!ok) {
+      for (int st = 0; st < SA; ++st) {
+        if (!((used >> st) & 1u)) continue;
+        for (uint32_t q = 0; q < (1u << 16); ++q)
+          if (mbar_try_wait(&afull_bar[st], (used_phase >> st) & 1u)) break;
+      }
+    }
+  } else if (warp < kProdWarps) {
+    // ----------------------------------------------------- weight producers
+    // Producer p (warps 1..nprod) loads weight sub-steps i with i % nprod == p.
+    if (warp <= a.nprod) {
+      const int p = warp - 1;
+      int owner = 0, stage = 0;
+      uint32_t phase = 0;
+      uint32_t used = 0, used_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
+        const int pt = tile / n_ct;
+        const int ct = tile - pt * n_ct;
+        const uint32_t km = tile_kmask(a, pt);
+        if (km == 0) continue;
+        for (int gh = 0; gh < n_gh && ok; ++gh) {
+          for (int gw = 0; gw < a.KW && ok; ++gw) {
+            for (int kc = 0; kc < a.n_kc && ok; ++kc) {
+              if (!((km >> kc) & 1u)) continue;
+              int tap = gh * a.KW + gw;
+              for (int j = 0; j < nsub; ++j, tap += a.KW) {
+                const bool mine = owner == p;
+                const int my_stage = stage;
+                const uint32_t my_phase = phase;
+                if (++owner == a.nprod) owner = 0;
+                if (++stage == SW) {
+                  stage = 0;
+                  phase ^= 1u;
+                }
+                if (!mine) continue;
+                if (!warp_wait_or_abort(&wempty_bar[my_stage], my_phase ^ 1u,
+                                        ERR_SITE_PRODUCER_EMPTY, abort_flag, a.backoff)) {
+                  ok = false;
+                  break;
+                }
+                if (lane == 0) {
+                  if (dbg & 1024) {
+                    mbar_arrive(&wfull_bar[my_stage]);
+                  } else {
+                    mbar_arrive_expect_tx(&wfull_bar[my_stage], W_BYTES);
+                    tma_load_2d(sW + (size_t)my_stage * W_BYTES, &tmW, &wfull_bar[my_stage],
+                                tap * a.Cin_p + kc * BK, ct * 128);
+                  }
+                }
+                __syncwarp();
+                used |= 1u << my_stage;
+                used_phase = (used_phase & ~(1u << my_stage)) | (my_phase << my_stage);
+              }
+            }
+          }
+        }
+      }
+      if (!ok) {
+        for (int st = 0; st < SW; ++st) {
+          if (!((used >> st) & 1u)) continue;
+          for (uint32_t q = 0; q < (1u << 16); ++q)
+            if (mbar_try_wait(&wfull_bar[st], (used_phase >> st) & 1u)) break;
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t x_step = (uint32_t)X_BYTES >> 4;
+      const uint32_t xa_step = (uint32_t)XA >> 4;
       const uint32_t w_step = (uint32_t)W_BYTES >> 4;
+      const uint32_t sub_step = ((uint32_t)(a.Wb * TP) * ROWB) >> 4;  // kh-box row shift
       const uint64_t x_desc0 = make_smem_desc(smem_u32(sX), ROWB);
       const uint64_t w_desc0 = make_smem_desc(smem_u32(sW), ROWB);
       const int ksteps = BK / 16;
-      const int n_tap = a.KH * a.KW;
-      int stage = 0;
-      uint32_t phase = 0;
+      int astage = 0, wstage = 0;
+      uint32_t aphase = 0, wphase = 0;
       uint64_t xd = x_desc0, wd = w_desc0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      const bool wt_tr = (dbg & 32) && blockIdx.x < 148;
+      long long t_a = 0, t_w = 0, t_t = 0, t_c;
+      const long long t_start = clock64();
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int pt = tile / n_ct;
         const uint32_t km = tile_kmask(a, pt);
+        if (wt_tr) t_c = clock64();
         if (!wait_or_abort(&tempty_bar[acc], acc_phase ^ 1u, ERR_SITE_MMA_TEMPTY, abort_flag)) {
           ok = false;
           break;
         }
+        if (wt_tr) t_t += clock64() - t_c;
         tc_fence_after();
         if (km == 0) {
           mbar_arrive(&tfull_bar[acc]);
         } else {
           const uint32_t d_tmem = tmem_base + (uint32_t)(acc * NR);
           uint32_t accum = 0u;
-          for (int tg = 0; tg < n_tap && ok; ++tg) {
-            for (int kc = 0; kc < a.n_kc; ++kc) {
+          const int n_g = n_gh * a.KW;
+          for (int g = 0; g < n_g && ok; ++g) {
+            for (int kc = 0; kc < a.n_kc && ok; ++kc) {
               if (!((km >> kc) & 1u)) continue;
-              if (!mbar_try_wait(&full_bar[stage], phase) &&
-                  !wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag)) {
+              if (wt_tr) t_c = clock64();
+              if (!mbar_try_wait(&afull_bar[astage], aphase) &&
+                  !wait_or_abort(&afull_bar[astage], aphase, ERR_SITE_MMA_FULL, abort_flag)) {
                 ok = false;
                 break;
               }
-              if (dbg & 1) {
-              } else if (ksteps == 4) issue_kchunk<4>(d_tmem, wd, xd, a.idesc, accum);
-              else if (ksteps == 2) issue_kchunk<2>(d_tmem, wd, xd, a.idesc, accum);
-              else issue_kchunk<1>(d_tmem, wd, xd, a.idesc, accum);
-              accum = 1u;
-              umma_commit(&empty_bar[stage]);
-              if (++stage == S) {
-                stage = 0;
-                phase ^= 1u;
+              if (wt_tr) t_a += clock64() - t_c;
+              if (!a.khbox) {
+                // paired stage: weight tile of the same stage index
+                const uint64_t wdp = w_desc0 + (uint64_t)((uint32_t)astage * w_step);
+                if (dbg & 1) {
+                } else if (ksteps == 4) issue_kchunk<4>(d_tmem, wdp, xd, a.idesc, accum);
+                else if (ksteps == 2) issue_kchunk<2>(d_tmem, wdp, xd, a.idesc, accum);
+                else issue_kchunk<1>(d_tmem, wdp, xd, a.idesc, accum);
+                accum = 1u;
+              }
+              uint64_t bd = xd;
+              for (int j = 0; j < (a.khbox ? nsub : 0); ++j, bd += sub_step) {
+                if (wt_tr) t_c = clock64();
+                if (!mbar_try_wait(&wfull_bar[wstage], wphase) &&
+                    !wait_or_abort(&wfull_bar[wstage], wphase, ERR_SITE_MMA_FULL, abort_flag)) {
+                  ok = false;
+                  break;
+                }
+                if (wt_tr) t_w += clock64() - t_c;
+                if (dbg & 1) {
+                } else if (ksteps == 4) issue_kchunk<4>(d_tmem, wd, bd, a.idesc, accum);
+                else if (ksteps == 2) issue_kchunk<2>(d_tmem, wd, bd, a.idesc, accum);
+                else issue_kchunk<1>(d_tmem, wd, bd, a.idesc, accum);
+                accum = 1u;
+                umma_commit(&wempty_bar[wstage]);
+                if (++wstage == SW) {
+                  wstage = 0;
+                  wphase ^= 1u;
+                  wd = w_desc0;
+                } else {
+                  wd += w_step;
+                }
+              }
+              if (!ok) break;
+              umma_commit(&aempty_bar[astage]);
+              if (++astage == SA) {
+                astage = 0;
+                aphase ^= 1u;
                 xd = x_desc0;
-                wd = w_desc0;
               } else {
-                xd += x_step;
-                wd += w_step;
+                xd += xa_step;
               }
             }
           }
@@ -957,10 +1122,17 @@ __global__ void __launch_bounds__(kTThreads, 1)
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
+      const long long t_loop = clock64() - t_start;
       umma_commit(done_bar);
       for (uint32_t p = 0; p < kMaxPolls; ++p)
         if (mbar_try_wait(done_bar, 0)) break;
       if ((dbg & 8) && blockIdx.x < 256) g_trace[blockIdx.x * 4 + 2] = globaltimer_ns();
+      if (wt_tr) {
+        g_trace[1024 + blockIdx.x * 4] = t_loop;
+        g_trace[1024 + blockIdx.x * 4 + 1] = t_a;
+        g_trace[1024 + blockIdx.x * 4 + 2] = t_w;
+        g_trace[1024 + blockIdx.x * 4 + 3] = t_t;
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -1084,9 +1256,9 @@ bool use_tmode(int64_t Cout) {
   return env != 0 && Cout % 128 == 0;
 }
 
-// Choose the pixel box (Wb x Hb x Bb = 128/TP, powers of two) that wastes the
-// fewest padded output pixels; ties go to the wider box (longer contiguous
-// rows for the output stores).
+// Choose the pixel box (Wb x Hb x Bb = P, powers of two) that wastes the
+// fewest padded output pixels; ties go to boxes inside one image, then to the
+// wider box (longer contiguous rows for the output stores).
 void choose_box(int P, int B, int Ho, int Wo, int stride, Geometry& g) {
   long best = -1;
   for (int wb = 1; wb <= P; wb <<= 1) {
@@ -1097,7 +1269,9 @@ void choose_box(int P, int B, int Ho, int Wo, int stride, Geometry& g) {
       if (bb > 256) continue;
       const long nwt = (Wo + wb - 1) / wb, nht = (Ho + hb - 1) / hb, nbt = (B + bb - 1) / bb;
       const long cost = nwt * nht * nbt;
-      if (best < 0 || cost < best || (cost == best && wb > g.Wb)) {
+      // ties: fewer images per tile (boxes stay inside one image), then wider
+      if (best < 0 || cost < best ||
+          (cost == best && (bb < g.Bb || (bb == g.Bb && wb > g.Wb)))) {
         best = cost;
         g.Wb = wb; g.Hb = hb; g.Bb = bb;
         g.n_wt = (int)nwt; g.n_ht = (int)nht; g.n_bt = (int)nbt;
@@ -1199,15 +1373,30 @@ int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, i
 template <int TP, int RES, bool FAST>
 int launch_t(const CUtensorMap& tmX, const CUtensorMap& tmW, ConvArgs args, int grid,
              cudaStream_t stream) {
-  const int per_stage = (args.NR + 128) * args.BK * 2;
-  const int fixed = 1024 + kTEpiWarps * kStageBytes + 256;
-  int stages = (kSmemBudget - fixed) / per_stage;
-  if (stages > 8) stages = 8;
-  if (args.stages > 1 && args.stages < stages) stages = args.stages;  // tuning override
-  if (stages < 2) return fail(CF_ERR_UNSUPPORTED, "conv tile does not fit shared memory");
-  args.stages = stages;
-  args.nprod = stages < kProdWarps ? stages : kProdWarps;
-  int smem = fixed + stages * per_stage;
+  const int w_bytes = 128 * args.BK * 2;
+  // 1 KB alignment slack, epilogue staging, up to 2*(8+8)+5 barriers + 2 words
+  const int fixed = 1024 + kTEpiWarps * kStageBytes + 512;
+  const int budget = kTSmemBudget - fixed;
+  int sa, sw;
+  if (args.khbox) {
+    sa = 2;
+    sw = (budget - sa * args.a_bytes) / w_bytes;
+  } else {
+    sa = sw = budget / (args.a_bytes + w_bytes);
+  }
+  if (sw > 8) sw = 8;
+  if (sa > 8) sa = 8;
+  if (args.stages > 1 && args.stages < sa) sa = args.stages;  // tuning override
+  if (sa < 2 || sw < 2) return fail(CF_ERR_UNSUPPORTED, "conv tile does not fit shared memory");
+  if (!args.khbox) sw = sa;
+  args.stages = sa;
+  args.wstages = sw;
+  // Round-robin producers may run at most one ring ahead only if there are
+  // no more of them than stages: kh-box mode has weight producers 1..3,
+  // paired mode producers 0..3.
+  if (args.khbox) args.nprod = sw < kProdWarps - 1 ? sw : kProdWarps - 1;
+  else args.nprod = sa < kProdWarps ? sa : kProdWarps;
+  int smem = fixed + sa * args.a_bytes + sw * w_bytes;
   if (smem < 120 * 1024) smem = 120 * 1024;  // one TMEM-owning CTA per SM
   static bool attr_set = false;
   if (!attr_set) {
@@ -1323,6 +1512,10 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   const int Wh = g.Wb + (int)KW - 1;
   const int halo_bytes = ((g.TP * Wh * (int)KH * g.BK * 2) + 1023) / 1024 * 1024;
   const int fixed_bytes = 1024 + kEpiBytes + 256;
+  static const int env_khbox = getenv("CATFUSE_CONV_KHBOX") ? atoi(getenv("CATFUSE_CONV_KHBOX")) : 1;
+  // The kh shift (Wb*TP rows) must keep the operand on a 1 KB swizzle boundary.
+  const int khbox = (g.tmode && env_khbox && stride == 1 && KH > 1 && g.Bb == 1 &&
+                     g.Hb + KH - 1 <= 256 && (g.Wb * g.TP * g.BK * 2) % 1024 == 0) ? 1 : 0;
   const int halo = (!g.tmode && env_halo && wres && stride == 1 && g.Hb == 1 && g.Bb == 1 &&
                     g.Wb * g.TP == 128 && g.TP >= 4 && g.BK == 64 && Wh <= 256 && KH <= 256 &&
                     fixed_bytes + wslab + 2 * halo_bytes <= kSmemBudget) ? 1 : 0;
@@ -1338,6 +1531,7 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
       box[2] = (cuuint32_t)Wh;
       box[3] = (cuuint32_t)KH;
     }
+    if (khbox) box[3] = (cuuint32_t)(g.Hb + KH - 1);
     cuuint32_t estr[5] = {1, 1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
     CUresult r = encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(x), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(g.BK * 2),
@@ -1397,7 +1591,12 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.Wh = Wh;
   static const int env_backoff = getenv("CATFUSE_CONV_BACKOFF") ? atoi(getenv("CATFUSE_CONV_BACKOFF")) : 256;
   args.backoff = env_backoff;
-  args.a_bytes = halo ? halo_bytes : 128 * g.BK * 2;
+  args.khbox = khbox;
+  if (g.tmode)
+    args.a_bytes = khbox ? (g.Hb + (int)KH - 1) * g.Wb * g.TP * g.BK * 2  // 1 KB multiple
+                         : g.NR * g.BK * 2;
+  else
+    args.a_bytes = halo ? halo_bytes : 128 * g.BK * 2;
   const int grid = args.n_tiles < sm_count() ? args.n_tiles : sm_count();
 
   for (int64_t t0 = 0; t0 < T; t0 += kMaxTP) {
