@@ -58,9 +58,10 @@ constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter
 constexpr int kConvThreads = 32 * (kProdWarps + 1 + kEpiWarps);
 constexpr int kEpiRowStride = 36;  // floats per transpose row (bank-conflict free)
 constexpr int kEpiBytes = kEpiWarps * 32 * kEpiRowStride * 4;
-// Channel-major kernel: three epilogue warps per TMEM lane quarter (its
-// epilogue is latency-bound; more resident warps hide the latency).
-constexpr int kTEpiWarps = 12;
+// Channel-major kernel: two epilogue warps per TMEM lane quarter (a third
+// one measured no faster and lowers the register cap below what the
+// residual epilogues need).
+constexpr int kTEpiWarps = 8;
 constexpr int kTSmemBudget = 227 * 1024;  // the whole opt-in shared memory of a CTA
 constexpr int kTThreads = 32 * (kProdWarps + 1 + kTEpiWarps);
 constexpr int kSmemBudget = 220 * 1024;
@@ -670,7 +671,11 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
                                             int bt, int p0, uint8_t* stage, int lane,
                                             long long* tr = nullptr) {
   constexpr int PP = 32 / TP;  // pixels in this chunk
-  constexpr bool kIdent = (RES != CF_RES_NONE && RES != CF_RES_Z_ONLY);
+  // Post-LIF combines (SEW ADD/AND/IAND) act on whole staged rows; only the
+  // add-before-LIF form needs the identity in the channel-per-lane layout.
+  constexpr bool kIdent = (RES == CF_RES_ADD_PRE);
+  constexpr bool kPost = (RES == CF_RES_ADD_POST || RES == CF_RES_AND_POST ||
+                          RES == CF_RES_IAND_POST);
   constexpr bool kLif = (RES != CF_RES_Z_ONLY);
   constexpr bool full_t = FULLT;  // all TP steps valid: straight-line recurrences
   // Row of this lane in the transposed phase: pixel rp, step rt.
@@ -754,9 +759,6 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
           o = z;
         } else {
           o = lif_any<FAST>(vv, z, a.lp);
-          if constexpr (RES == CF_RES_ADD_POST) o += idv[j];
-          else if constexpr (RES == CF_RES_AND_POST) o *= idv[j];
-          else if constexpr (RES == CF_RES_IAND_POST) o = idv[j] * (1.f - o);
         }
         hrow[j * (kStageRowB / 2)] = __float2half_rn(o);
       }
@@ -773,9 +775,28 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
   if (tr) tr[1] = clock64();
   __syncwarp();
   if (rok) {
+    uint4 o4[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o4[k] = srow[k];
+    if constexpr (kPost) {
+      // spikes {0,1} combined with identity spikes {0,1,2}: exact in fp16
+      const uint4* src = reinterpret_cast<const uint4*>(a.identity + row_off);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 i4 = src[k];
+        __half2* s2 = reinterpret_cast<__half2*>(&o4[k]);
+        const __half2* d2 = reinterpret_cast<const __half2*>(&i4);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          if constexpr (RES == CF_RES_ADD_POST) s2[m] = __hadd2(s2[m], d2[m]);
+          else if constexpr (RES == CF_RES_AND_POST) s2[m] = __hmul2(s2[m], d2[m]);
+          else s2[m] = __hmul2(d2[m], __hsub2(__float2half2_rn(1.f), s2[m]));
+        }
+      }
+    }
     uint4* dst = reinterpret_cast<uint4*>(a.out + row_off);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) dst[k] = srow[k];
+    for (int k = 0; k < 4; ++k) dst[k] = o4[k];
   }
   __syncwarp();  // the staging rows are reused by the next chunk
   if (tr) tr[2] = clock64();
@@ -1137,13 +1158,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     // Warp e reads TMEM lane quarter q = warp % 4 (channels q*32 + lane of the
-    // tile) and the 32-column chunks k, k+3, ... with k = e / 4.
+    // tile) and the 32-column chunks k, k+E, ... with k = e / 4, E = warps per quarter.
+    constexpr int E = kTEpiWarps / 4;
     const int e = warp - kEpiWarp0;
     const int q = warp & 3;
     const int k = e >> 2;
     const int n_chunk = NR >> 5;
     int last_chunk = k;
-    while (last_chunk + 3 < n_chunk) last_chunk += 3;
+    while (last_chunk + E < n_chunk) last_chunk += E;
     uint8_t* stage = sStage + e * kStageBytes;
     int ep_n = 0;
     int acc = 0;
@@ -1164,9 +1186,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
       tc_fence_after();
       const bool tr = (dbg & 16) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_n < 8;
       if (tr) g_trace[1024 + ep_n * 16] = clock64();
-      for (int ch = k; ch < n_chunk; ch += 3) {
+      for (int ch = k; ch < n_chunk; ch += E) {
         const int col = ch * 32;
-        const int c0 = (ch / 3) * 32;  // trace slot
+        const int c0 = (ch / E) * 32;  // trace slot
         float r[32];
         if (has_acc) {
           tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * NR + col), r);
