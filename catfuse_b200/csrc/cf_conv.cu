@@ -101,8 +101,8 @@ struct ConvArgs {
   int backoff;      // ns of sleep between polls for the non-critical waiters
   int tmode;        // 1: channel-major kernel (conv_t_kernel)
   int khbox;        // channel-major: one activation box covers all kh taps of a kw column
-  int wstages;      // channel-major: weight ring depth (act ring depth = stages)
   int NR;           // channel-major kernel: pixel x time rows per tile (MMA N)
+  int MT;           // channel-major kernel: output channels per tile (MMA M), 128 or 64
   int lwb, lhb;     // log2 of Wb and Hb
   LifParams lp;
 };
@@ -656,67 +656,104 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 // affine as two per-thread scalars and no shared-memory transpose.
 // Warp roles and the producer/MMA pipeline are those of conv_bn_lif_kernel.
 // --------------------------------------------------------------------------
-constexpr int kStageRowB = 80;  // bytes per staging row: 32 halves + pad (16-B aligned)
-constexpr int kStageBytes = 32 * kStageRowB;
+// Epilogue staging of one warp.  M=128 tiles: 32 rows (pixel-time columns of
+// the chunk) x 32 channels, row stride 80 B.  M=64 tiles: two sets (one per
+// half-warp) of 32 rows x 16 channels, row stride 48 B, the second set 32 B
+// further on so the two half-warps' 2-byte writes hit disjoint banks.
+template <int MT>
+__device__ __forceinline__ int stage_row_off(int r) {
+  if constexpr (MT == 128) return r * 80;
+  else return (r >> 5) * (32 * 48 + 32) + (r & 31) * 48;
+}
+constexpr int kStageBytes = 3200;  // >= max(32 * 80, 2 * (32 * 48 + 32)), 16-B multiple
+// Channel-major kernel: 1 KB alignment slack, epilogue staging, up to 2*8+5
+// barriers and two words.
+constexpr int kTFixedBytes = 1024 + kTEpiWarps * kStageBytes + 256;
 
-// Epilogue of one 32-column chunk of the channel-major accumulator.  Lane =
-// output channel co; r[pp*TP + t] = z of pixel p0+pp, step t.  The LIF runs
-// in these registers; the fp16 results go through the warp's staging rows
-// (row = pixel-time column, 32 channels) so that each lane then writes one
-// (pixel, step) row of 32 channels as four 16-byte stores.  Identity spikes
-// come in the same way in reverse.
-template <int TP, int RES, bool FAST, bool FULLT>
+// Epilogue of one chunk of the channel-major accumulator.  This lane owns
+// channel co (local index cl) and the 32 pixel-time columns cb .. cb+31 with
+// cb = col0 (M=128) or col0 + 32 * (lane / 16) (M=64): r[pp*TP + t] = z of
+// pixel cb/TP + pp, step t.  The LIF runs in these registers; the fp16
+// results go through the staging rows (row = column - col0) so that each lane
+// then writes whole (pixel, step) rows of the chunk's channels with 16-byte
+// stores.  Post-LIF SEW combines are applied to those rows; the add-before-LIF
+// identity comes in the same way in reverse.
+template <int TP, int RES, bool FAST, bool FULLT, int MT>
 __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[32], int co,
                                             int co_base, float sc, float sh, int wt, int ht,
-                                            int bt, int p0, uint8_t* stage, int lane,
+                                            int bt, int col0, uint8_t* stage, int lane,
                                             long long* tr = nullptr) {
-  constexpr int PP = 32 / TP;  // pixels in this chunk
-  // Post-LIF combines (SEW ADD/AND/IAND) act on whole staged rows; only the
-  // add-before-LIF form needs the identity in the channel-per-lane layout.
+  constexpr int PP = 32 / TP;               // pixels per lane
+  constexpr int CPR = MT == 128 ? 32 : 16;  // channels per staged row
+  constexpr int NQ = CPR / 8;               // 16-byte pieces per row
+  constexpr int RL = MT == 128 ? 1 : 2;     // staged rows written out per lane
   constexpr bool kIdent = (RES == CF_RES_ADD_PRE);
   constexpr bool kPost = (RES == CF_RES_ADD_POST || RES == CF_RES_AND_POST ||
                           RES == CF_RES_IAND_POST);
   constexpr bool kLif = (RES != CF_RES_Z_ONLY);
   constexpr bool full_t = FULLT;  // all TP steps valid: straight-line recurrences
-  // Row of this lane in the transposed phase: pixel rp, step rt.
-  const int rp = lane / TP, rt = lane - (lane / TP) * TP;
-  int64_t rpix;
-  bool rok;
-  {
-    const int p = p0 + rp;
+  const int h = MT == 128 ? 0 : (lane >> 4);
+  const int cl = MT == 128 ? lane : (lane & 15);
+  const int p0 = (col0 + 32 * h) / TP;
+
+  // Output rows of this lane in the transposed phase: staged row i*32 + lane
+  // = column col0 + i*32 + lane.
+  int64_t row_off[RL];
+  bool rok[RL];
+#pragma unroll
+  for (int i = 0; i < RL; ++i) {
+    const int c = col0 + i * 32 + lane;
+    const int p = c / TP, t = c - (c / TP) * TP;
     const int wo = (wt << a.lwb) + (p & ((1 << a.lwb) - 1));
     const int ho = (ht << a.lhb) + ((p >> a.lwb) & ((1 << a.lhb) - 1));
     const int b = bt * a.Bb + (p >> (a.lwb + a.lhb));
-    rok = wo < a.Wo && ho < a.Ho && b < a.B && rt < a.tcount;
-    rpix = ((int64_t)b * a.Ho + ho) * a.Wo + wo;
+    rok[i] = wo < a.Wo && ho < a.Ho && b < a.B && t < a.tcount;
+    const int64_t pix = ((int64_t)b * a.Ho + ho) * a.Wo + wo;
+    row_off[i] = (pix * a.T + a.t0 + t) * a.Cout + co_base;
   }
-  const int64_t row_off = (rpix * a.T + a.t0 + rt) * a.Cout + co_base;
-  uint4* srow = reinterpret_cast<uint4*>(stage + lane * kStageRowB);
-  const __half* scol = reinterpret_cast<const __half*>(stage) + lane;  // + row * 40
+
+  // Post-LIF combines: fetch this lane's identity rows now so their latency
+  // overlaps the recurrence below.
+  uint4 idr[kPost ? RL : 1][kPost ? NQ : 1];
+  if constexpr (kPost) {
+#pragma unroll
+    for (int i = 0; i < RL; ++i) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.identity + row_off[i]);
+#pragma unroll
+      for (int k = 0; k < NQ; ++k) idr[i][k] = rok[i] ? src[k] : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
 
   float idv[kIdent ? 32 : 1];
   if constexpr (kIdent) {
-    uint4 q4[4] = {};
-    if (rok) {
-      const uint4* src = reinterpret_cast<const uint4*>(a.identity + row_off);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) q4[k] = src[k];
+    for (int i = 0; i < RL; ++i) {
+      uint4 q4[NQ];
+#pragma unroll
+      for (int k = 0; k < NQ; ++k) q4[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (rok[i]) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.identity + row_off[i]);
+#pragma unroll
+        for (int k = 0; k < NQ; ++k) q4[k] = src[k];
+      }
+      uint4* srow = reinterpret_cast<uint4*>(stage + stage_row_off<MT>(i * 32 + lane));
+#pragma unroll
+      for (int k = 0; k < NQ; ++k) srow[k] = q4[k];
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) srow[k] = q4[k];
     __syncwarp();
 #pragma unroll
-    for (int j = 0; j < 32; ++j) idv[j] = __half2float(scol[j * (kStageRowB / 2)]);
+    for (int j = 0; j < 32; ++j)
+      idv[j] = __half2float(
+          *reinterpret_cast<const __half*>(stage + stage_row_off<MT>(h * 32 + j) + cl * 2));
     __syncwarp();
   }
 
-  // Membranes of this lane's channel for the chunk's pixels (coalesced over
-  // the warp's 32 channels), all issued before any store.
+  // Membranes of this lane's channel for its pixels, all issued before any store.
   int64_t pix[PP];
   bool ok[PP];
   float v[PP];
   if ((1 << a.lwb) >= PP) {
-    // The chunk's pixels are consecutive in one output row.
+    // The lane's pixels are consecutive in one output row.
     const int wo0 = (wt << a.lwb) + (p0 & ((1 << a.lwb) - 1));
     const int ho = (ht << a.lhb) + ((p0 >> a.lwb) & ((1 << a.lhb) - 1));
     const int b = bt * a.Bb + (p0 >> (a.lwb + a.lhb));
@@ -743,7 +780,7 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
     for (int pp = 0; pp < PP; ++pp) v[pp] = (a.v_in && ok[pp]) ? a.v_in[pix[pp] * a.Cout + co] : 0.f;
   }
 
-  __half* hrow = reinterpret_cast<__half*>(stage) + lane;
+  uint8_t* hbase = stage + cl * 2;
   if (tr) tr[0] = clock64();
 #pragma unroll
   for (int pp = 0; pp < PP; ++pp) {
@@ -760,7 +797,7 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
         } else {
           o = lif_any<FAST>(vv, z, a.lp);
         }
-        hrow[j * (kStageRowB / 2)] = __float2half_rn(o);
+        *reinterpret_cast<__half*>(hbase + stage_row_off<MT>(h * 32 + j)) = __float2half_rn(o);
       }
     }
     if (kLif) v[pp] = vv;
@@ -774,16 +811,18 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
   }
   if (tr) tr[1] = clock64();
   __syncwarp();
-  if (rok) {
-    uint4 o4[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) o4[k] = srow[k];
+  for (int i = 0; i < RL; ++i) {
+    if (!rok[i]) continue;
+    const uint4* srow = reinterpret_cast<const uint4*>(stage + stage_row_off<MT>(i * 32 + lane));
+    uint4 o4[NQ];
+#pragma unroll
+    for (int k = 0; k < NQ; ++k) o4[k] = srow[k];
     if constexpr (kPost) {
       // spikes {0,1} combined with identity spikes {0,1,2}: exact in fp16
-      const uint4* src = reinterpret_cast<const uint4*>(a.identity + row_off);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint4 i4 = src[k];
+      for (int k = 0; k < NQ; ++k) {
+        const uint4 i4 = idr[i][k];
         __half2* s2 = reinterpret_cast<__half2*>(&o4[k]);
         const __half2* d2 = reinterpret_cast<const __half2*>(&i4);
 #pragma unroll
@@ -794,9 +833,9 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
         }
       }
     }
-    uint4* dst = reinterpret_cast<uint4*>(a.out + row_off);
+    uint4* dst = reinterpret_cast<uint4*>(a.out + row_off[i]);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) dst[k] = o4[k];
+    for (int k = 0; k < NQ; ++k) dst[k] = o4[k];
   }
   __syncwarp();  // the staging rows are reused by the next chunk
   if (tr) tr[2] = clock64();
@@ -809,30 +848,31 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const int dbg = CF_CONV_DEBUG_KNOBS ? a.debug : 0;  // see ConvArgs::debug
   const int BK = a.BK;
   const int NR = a.NR;
-  const int XA = a.a_bytes;          // activation box of one act stage
-  const int W_BYTES = 128 * BK * 2;  // weight tile of one weight stage
+  const int XA = a.a_bytes;          // activation box of one stage
+  const int MT = a.MT;               // output channels per tile (MMA M): 128 or 64
+  const int W_BYTES = MT * BK * 2;   // one weight tile
   const uint32_t ROWB = (uint32_t)BK * 2;
-  const int SA = a.stages;           // activation stages
-  const int SW = a.wstages;          // weight stages
-  const int n_ct = a.n_ntiles;       // output-channel tiles of 128
-  // Act steps walk (gh, gw, kc); each serves nsub weight sub-steps.  In the
-  // kh-box mode (stride 1, tile inside one image) one activation box of
-  // Hb+KH-1 rows covers all kh taps of a kw column: tap (kh, kw) reads it
-  // from row kh*Wb*TP on, and the act step loop has gh = 0 only.
+  const int S = a.stages;
+  const int n_ct = a.n_ntiles;       // output-channel tiles
+  // A stage carries one activation box and the nsub weight tiles it serves.
+  // Steps walk (gh, gw, kc).  In the kh-box mode (stride 1, tile inside one
+  // image) one activation box of Hb+KH-1 rows covers all kh taps of a kw
+  // column: tap (kh, kw) reads it from row kh*Wb*TP on, the step loop has
+  // gh = 0 only and the stage holds KH weight tiles.  One barrier wait and one
+  // commit then cover KH*BK/16 MMAs.
   const int n_gh = a.khbox ? 1 : a.KH;
   const int nsub = a.khbox ? a.KH : 1;
+  const int WSB = nsub * W_BYTES;    // weight bytes of one stage
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = smem;
-  uint8_t* sW = sX + (size_t)SA * XA;
-  uint8_t* sStage = sW + (size_t)SW * W_BYTES;  // epilogue staging, kStageBytes per warp
-  uint64_t* afull_bar = reinterpret_cast<uint64_t*>(sStage + kTEpiWarps * kStageBytes);
-  uint64_t* aempty_bar = afull_bar + SA;
-  uint64_t* wfull_bar = aempty_bar + SA;
-  uint64_t* wempty_bar = wfull_bar + SW;
-  uint64_t* tfull_bar = wempty_bar + SW;
+  uint8_t* sW = sX + (size_t)S * XA;
+  uint8_t* sStage = sW + (size_t)S * WSB;  // epilogue staging, kStageBytes per warp
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStage + kTEpiWarps * kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* done_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -843,13 +883,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
   if ((dbg & 8) && threadIdx.x == 0 && blockIdx.x < 256) g_trace[blockIdx.x * 4] = globaltimer_ns();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SA; ++s) {
-      mbar_init(&afull_bar[s], 1);
-      mbar_init(&aempty_bar[s], 1);
-    }
-    for (int s = 0; s < SW; ++s) {
-      mbar_init(&wfull_bar[s], 1);
-      mbar_init(&wempty_bar[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
@@ -873,10 +909,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   if ((dbg & 8) && threadIdx.x == 0 && blockIdx.x < 256) g_trace[blockIdx.x * 4 + 1] = globaltimer_ns();
 
-  if (!a.khbox && warp < kProdWarps) {
-    // ---------------------------------------------- paired producers (warps 0-3)
-    // Stage s of both rings carries one (tap, chunk): activation tile and
-    // weight tile on afull[s]; producer p issues k-iterations i % nprod == p.
+  if (warp < kProdWarps) {
+    // ------------------------------------------------------------ producers
+    // Producer p issues the steps i with i % nprod == p (stage i % S, phase
+    // (i / S) & 1): one activation box and nsub weight tiles on full[stage].
     if (warp < a.nprod) {
       const int p = warp;
       int owner = 0, stage = 0;
@@ -894,34 +930,35 @@ __global__ void __launch_bounds__(kTThreads, 1)
         const int b0 = bt * a.Bb;
         const uint32_t km = tile_kmask(a, pt);
         if (km == 0) continue;
-        int tap = 0;
-        for (int kh = 0; kh < a.KH && ok; ++kh) {
-          for (int kw = 0; kw < a.KW && ok; ++kw, ++tap) {
+        for (int gh = 0; gh < n_gh && ok; ++gh) {
+          for (int gw = 0; gw < a.KW && ok; ++gw) {
             for (int kc = 0; kc < a.n_kc; ++kc) {
               if (!((km >> kc) & 1u)) continue;
               const bool mine = owner == p;
               const int my_stage = stage;
               const uint32_t my_phase = phase;
               if (++owner == a.nprod) owner = 0;
-              if (++stage == SA) {
+              if (++stage == S) {
                 stage = 0;
                 phase ^= 1u;
               }
               if (!mine) continue;
-              if (!warp_wait_or_abort(&aempty_bar[my_stage], my_phase ^ 1u,
+              if (!warp_wait_or_abort(&empty_bar[my_stage], my_phase ^ 1u,
                                       ERR_SITE_PRODUCER_EMPTY, abort_flag, a.backoff)) {
                 ok = false;
                 break;
               }
               if (lane == 0) {
                 if (dbg & 1024) {
-                  mbar_arrive(&afull_bar[my_stage]);
+                  mbar_arrive(&full_bar[my_stage]);
                 } else {
-                  mbar_arrive_expect_tx(&afull_bar[my_stage], XA + W_BYTES);
-                  tma_load_5d(sX + (size_t)my_stage * XA, &tmX, &afull_bar[my_stage], kc * BK,
-                              a.t0, wi0 + kw, hi0 + kh, b0);
-                  tma_load_2d(sW + (size_t)my_stage * W_BYTES, &tmW, &afull_bar[my_stage],
-                              tap * a.Cin_p + kc * BK, ct * 128);
+                  mbar_arrive_expect_tx(&full_bar[my_stage], XA + WSB);
+                  tma_load_5d(sX + (size_t)my_stage * XA, &tmX, &full_bar[my_stage], kc * BK,
+                              a.t0, wi0 + gw, hi0 + gh, b0);
+                  int tap = gh * a.KW + gw;
+                  for (int j = 0; j < nsub; ++j, tap += a.KW)
+                    tma_load_2d(sW + (size_t)my_stage * WSB + (size_t)j * W_BYTES, &tmW,
+                                &full_bar[my_stage], tap * a.Cin_p + kc * BK, ct * MT);
                 }
               }
               __syncwarp();
@@ -932,121 +969,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
         }
       }
       if (!ok) {
-        for (int st = 0; st < SA; ++st) {
+        for (int st = 0; st < S; ++st) {
           if (!((used >> st) & 1u)) continue;
           for (uint32_t q = 0; q < (1u << 16); ++q)
-            if (mbar_try_wait(&afull_bar[st], (used_phase >> st) & 1u)) break;
-        }
-      }
-    }
-  } else if (warp == 0) {
-    // ------------------------------------------------- activation producer
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t used = 0, used_phase = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
-      const int pt = tile / n_ct;
-      const int wt = pt % a.n_wt;
-      const int ht = (pt / a.n_wt) % a.n_ht;
-      const int bt = pt / (a.n_wt * a.n_ht);
-      const int wi0 = wt * a.Wb * a.stride - a.pad;
-      const int hi0 = ht * a.Hb * a.stride - a.pad;
-      const int b0 = bt * a.Bb;
-      const uint32_t km = tile_kmask(a, pt);
-      if (km == 0) continue;
-      for (int gh = 0; gh < n_gh && ok; ++gh) {
-        for (int gw = 0; gw < a.KW && ok; ++gw) {
-          for (int kc = 0; kc < a.n_kc; ++kc) {
-            if (!((km >> kc) & 1u)) continue;
-            if (!warp_wait_or_abort(&aempty_bar[stage], phase ^ 1u, ERR_SITE_PRODUCER_EMPTY,
-                                    abort_flag, a.backoff)) {
-              ok = false;
-              break;
-            }
-            if (lane == 0) {
-              if (dbg & 1024) {
-                mbar_arrive(&afull_bar[stage]);
-              } else {
-                mbar_arrive_expect_tx(&afull_bar[stage], XA);
-                tma_load_5d(sX + (size_t)stage * XA, &tmX, &afull_bar[stage], kc * BK, a.t0,
-                            wi0 + gw, hi0 + gh, b0);
-              }
-            }
-            __syncwarp();
-            used |= 1u << stage;
-            used_phase = (used_phase & ~(1u << stage)) | (phase << stage);
-            if (++stage == SA) {
-              stage = 0;
-              phase ^= 1u;
-            }
-          }
-        }
-      }
-    }
-    if (!ok) {
-      for (int st = 0; st < SA; ++st) {
-        if (!((used >> st) & 1u)) continue;
-        for (uint32_t q = 0; q < (1u << 16); ++q)
-          if (mbar_try_wait(&afull_bar[st], (used_phase >> st) & 1u)) break;
-      }
-    }
-  } else if (warp < kProdWarps) {
-    // ----------------------------------------------------- weight producers
-    // Producer p (warps 1..nprod) loads weight sub-steps i with i % nprod == p.
-    if (warp <= a.nprod) {
-      const int p = warp - 1;
-      int owner = 0, stage = 0;
-      uint32_t phase = 0;
-      uint32_t used = 0, used_phase = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
-        const int pt = tile / n_ct;
-        const int ct = tile - pt * n_ct;
-        const uint32_t km = tile_kmask(a, pt);
-        if (km == 0) continue;
-        for (int gh = 0; gh < n_gh && ok; ++gh) {
-          for (int gw = 0; gw < a.KW && ok; ++gw) {
-            for (int kc = 0; kc < a.n_kc && ok; ++kc) {
-              if (!((km >> kc) & 1u)) continue;
-              int tap = gh * a.KW + gw;
-              for (int j = 0; j < nsub; ++j, tap += a.KW) {
-                const bool mine = owner == p;
-                const int my_stage = stage;
-                const uint32_t my_phase = phase;
-                if (++owner == a.nprod) owner = 0;
-                if (++stage == SW) {
-                  stage = 0;
-                  phase ^= 1u;
-                }
-                if (!mine) continue;
-                if (!warp_wait_or_abort(&wempty_bar[my_stage], my_phase ^ 1u,
-                                        ERR_SITE_PRODUCER_EMPTY, abort_flag, a.backoff)) {
-                  ok = false;
-                  break;
-                }
-                if (lane == 0) {
-                  if (dbg & 1024) {
-                    mbar_arrive(&wfull_bar[my_stage]);
-                  } else {
-                    mbar_arrive_expect_tx(&wfull_bar[my_stage], W_BYTES);
-                    tma_load_2d(sW + (size_t)my_stage * W_BYTES, &tmW, &wfull_bar[my_stage],
-                                tap * a.Cin_p + kc * BK, ct * 128);
-                  }
-                }
-                __syncwarp();
-                used |= 1u << my_stage;
-                used_phase = (used_phase & ~(1u << my_stage)) | (my_phase << my_stage);
-              }
-            }
-          }
-        }
-      }
-      if (!ok) {
-        for (int st = 0; st < SW; ++st) {
-          if (!((used >> st) & 1u)) continue;
-          for (uint32_t q = 0; q < (1u << 16); ++q)
-            if (mbar_try_wait(&wfull_bar[st], (used_phase >> st) & 1u)) break;
+            if (mbar_try_wait(&full_bar[st], (used_phase >> st) & 1u)) break;
         }
       }
     }
@@ -1054,19 +980,20 @@ __global__ void __launch_bounds__(kTThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t xa_step = (uint32_t)XA >> 4;
+      const uint32_t ws_step = (uint32_t)WSB >> 4;
       const uint32_t w_step = (uint32_t)W_BYTES >> 4;
       const uint32_t sub_step = ((uint32_t)(a.Wb * TP) * ROWB) >> 4;  // kh-box row shift
       const uint64_t x_desc0 = make_smem_desc(smem_u32(sX), ROWB);
       const uint64_t w_desc0 = make_smem_desc(smem_u32(sW), ROWB);
       const int ksteps = BK / 16;
-      int astage = 0, wstage = 0;
-      uint32_t aphase = 0, wphase = 0;
+      int stage = 0;
+      uint32_t phase = 0;
       uint64_t xd = x_desc0, wd = w_desc0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       const bool wt_tr = (dbg & 32) && blockIdx.x < 148;
-      long long t_a = 0, t_w = 0, t_t = 0, t_c;
+      long long t_a = 0, t_t = 0, t_c = 0;
       const long long t_start = clock64();
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int pt = tile / n_ct;
@@ -1085,55 +1012,34 @@ __global__ void __launch_bounds__(kTThreads, 1)
           uint32_t accum = 0u;
           const int n_g = n_gh * a.KW;
           for (int g = 0; g < n_g && ok; ++g) {
-            for (int kc = 0; kc < a.n_kc && ok; ++kc) {
+            for (int kc = 0; kc < a.n_kc; ++kc) {
               if (!((km >> kc) & 1u)) continue;
               if (wt_tr) t_c = clock64();
-              if (!mbar_try_wait(&afull_bar[astage], aphase) &&
-                  !wait_or_abort(&afull_bar[astage], aphase, ERR_SITE_MMA_FULL, abort_flag)) {
+              if (!mbar_try_wait(&full_bar[stage], phase) &&
+                  !wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag)) {
                 ok = false;
                 break;
               }
               if (wt_tr) t_a += clock64() - t_c;
-              if (!a.khbox) {
-                // paired stage: weight tile of the same stage index
-                const uint64_t wdp = w_desc0 + (uint64_t)((uint32_t)astage * w_step);
-                if (dbg & 1) {
-                } else if (ksteps == 4) issue_kchunk<4>(d_tmem, wdp, xd, a.idesc, accum);
-                else if (ksteps == 2) issue_kchunk<2>(d_tmem, wdp, xd, a.idesc, accum);
-                else issue_kchunk<1>(d_tmem, wdp, xd, a.idesc, accum);
-                accum = 1u;
-              }
-              uint64_t bd = xd;
-              for (int j = 0; j < (a.khbox ? nsub : 0); ++j, bd += sub_step) {
-                if (wt_tr) t_c = clock64();
-                if (!mbar_try_wait(&wfull_bar[wstage], wphase) &&
-                    !wait_or_abort(&wfull_bar[wstage], wphase, ERR_SITE_MMA_FULL, abort_flag)) {
-                  ok = false;
-                  break;
-                }
-                if (wt_tr) t_w += clock64() - t_c;
-                if (dbg & 1) {
-                } else if (ksteps == 4) issue_kchunk<4>(d_tmem, wd, bd, a.idesc, accum);
-                else if (ksteps == 2) issue_kchunk<2>(d_tmem, wd, bd, a.idesc, accum);
-                else issue_kchunk<1>(d_tmem, wd, bd, a.idesc, accum);
-                accum = 1u;
-                umma_commit(&wempty_bar[wstage]);
-                if (++wstage == SW) {
-                  wstage = 0;
-                  wphase ^= 1u;
-                  wd = w_desc0;
-                } else {
-                  wd += w_step;
+              if (!(dbg & 1)) {
+                uint64_t bd = xd, ad = wd;
+                for (int j = 0; j < nsub; ++j, bd += sub_step, ad += w_step) {
+                  if (ksteps == 4) issue_kchunk<4>(d_tmem, ad, bd, a.idesc, accum);
+                  else if (ksteps == 2) issue_kchunk<2>(d_tmem, ad, bd, a.idesc, accum);
+                  else issue_kchunk<1>(d_tmem, ad, bd, a.idesc, accum);
+                  accum = 1u;
                 }
               }
-              if (!ok) break;
-              umma_commit(&aempty_bar[astage]);
-              if (++astage == SA) {
-                astage = 0;
-                aphase ^= 1u;
+              if (dbg & 4) mbar_arrive(&empty_bar[stage]);
+              else umma_commit(&empty_bar[stage]);
+              if (++stage == S) {
+                stage = 0;
+                phase ^= 1u;
                 xd = x_desc0;
+                wd = w_desc0;
               } else {
                 xd += xa_step;
+                wd += ws_step;
               }
             }
           }
@@ -1151,19 +1057,23 @@ __global__ void __launch_bounds__(kTThreads, 1)
       if (wt_tr) {
         g_trace[1024 + blockIdx.x * 4] = t_loop;
         g_trace[1024 + blockIdx.x * 4 + 1] = t_a;
-        g_trace[1024 + blockIdx.x * 4 + 2] = t_w;
+        g_trace[1024 + blockIdx.x * 4 + 2] = 0;
         g_trace[1024 + blockIdx.x * 4 + 3] = t_t;
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Warp e reads TMEM lane quarter q = warp % 4 (channels q*32 + lane of the
-    // tile) and the 32-column chunks k, k+E, ... with k = e / 4, E = warps per quarter.
+    // Warp e reads TMEM lane quarter q = warp % 4 and the column chunks k,
+    // k+E, ... with k = e / 4, E = warps per quarter.  M=128: the quarter's 32
+    // lanes are channels q*32 + lane, a chunk is 32 columns.  M=64: lanes 0-15
+    // of the quarter hold channels q*16 + 0..15, a chunk is 64 columns and each
+    // half-warp takes 32 of them (tcgen05.ld 16x32bx2).
     constexpr int E = kTEpiWarps / 4;
     const int e = warp - kEpiWarp0;
     const int q = warp & 3;
     const int k = e >> 2;
-    const int n_chunk = NR >> 5;
+    const int CW = MT == 128 ? 32 : 64;  // columns per chunk
+    const int n_chunk = NR / CW;
     int last_chunk = k;
     while (last_chunk + E < n_chunk) last_chunk += E;
     uint8_t* stage = sStage + e * kStageBytes;
@@ -1177,7 +1087,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
       const int ht = (pt / a.n_wt) % a.n_ht;
       const int bt = pt / (a.n_wt * a.n_ht);
       const bool has_acc = tile_kmask(a, pt) != 0;
-      const int co = ct * 128 + q * 32 + lane;
+      const int co_base = ct * MT + q * (MT / 4);
+      const int co = co_base + (MT == 128 ? lane : (lane & 15));
       const float sc = a.scale ? __ldg(a.scale + co) : 1.f;
       const float sh = a.shift ? __ldg(a.shift + co) : 0.f;
       if (!warp_wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag,
@@ -1187,14 +1098,17 @@ __global__ void __launch_bounds__(kTThreads, 1)
       const bool tr = (dbg & 16) && blockIdx.x == 0 && e == 0 && lane == 0 && ep_n < 8;
       if (tr) g_trace[1024 + ep_n * 16] = clock64();
       for (int ch = k; ch < n_chunk; ch += E) {
-        const int col = ch * 32;
+        const int col = ch * CW;
         const int c0 = (ch / E) * 32;  // trace slot
         float r[32];
-        if (has_acc) {
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * NR + col), r);
-        } else {
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * NR + col);
+        if (!has_acc) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = 0.f;
+        } else if (MT == 128) {
+          tmem_ld32(taddr, r);
+        } else {
+          tmem_ld16x2_32(taddr, r);
         }
         if (tr) g_trace[1024 + ep_n * 16 + 1 + (c0 / 32) * 2] = clock64();
         if (ch == last_chunk) {
@@ -1204,13 +1118,21 @@ __global__ void __launch_bounds__(kTThreads, 1)
           if (lane == 0) mbar_arrive(&tempty_bar[acc]);
         }
         if (dbg & 2) {
-        } else if (a.tcount == TP) {
-          epi_chunk_t<TP, RES, FAST, true>(a, r, co, ct * 128 + q * 32, sc, sh, wt, ht, bt,
-                                           col / TP, stage, lane,
-                                           tr ? &g_trace[1200 + ep_n * 16 + (c0 / 32) * 3] : nullptr);
+        } else if (MT == 128) {
+          if (a.tcount == TP)
+            epi_chunk_t<TP, RES, FAST, true, 128>(a, r, co, co_base, sc, sh, wt, ht, bt, col,
+                                                  stage, lane,
+                                                  tr ? &g_trace[1200 + ep_n * 16 + (c0 / 32) * 3] : nullptr);
+          else
+            epi_chunk_t<TP, RES, FAST, false, 128>(a, r, co, co_base, sc, sh, wt, ht, bt, col,
+                                                   stage, lane);
         } else {
-          epi_chunk_t<TP, RES, FAST, false>(a, r, co, ct * 128 + q * 32, sc, sh, wt, ht, bt,
-                                            col / TP, stage, lane);
+          if (a.tcount == TP)
+            epi_chunk_t<TP, RES, FAST, true, 64>(a, r, co, co_base, sc, sh, wt, ht, bt, col,
+                                                 stage, lane);
+          else
+            epi_chunk_t<TP, RES, FAST, false, 64>(a, r, co, co_base, sc, sh, wt, ht, bt, col,
+                                                  stage, lane);
         }
         if (tr) g_trace[1024 + ep_n * 16 + 2 + (c0 / 32) * 2] = clock64();
       }
@@ -1272,10 +1194,16 @@ struct Geometry {
 };
 
 // The channel-major kernel serves every layer whose output channels come in
-// whole 128-channel tiles.
-bool use_tmode(int64_t Cout) {
+// whole 128-channel tiles (M = 128) or 64-channel tiles (M = 64, half the
+// per-MAC rate of M = 128 but still 128 tensor cycles per N = 256 MMA, and
+// 80 instead of 192 B/clk of operand reads compared with N = 64 tiles of the
+// pixel-major kernel).
+// Narrow-input 64-channel layers (the stem's im2col with K <= 32) have too
+// little MMA work per tile to hide the channel-major epilogue and stay on the
+// pixel-major kernel.
+bool use_tmode(int64_t Cout, int64_t Cin_p) {
   static const int env = getenv("CATFUSE_CONV_TMODE") ? atoi(getenv("CATFUSE_CONV_TMODE")) : 1;
-  return env != 0 && Cout % 128 == 0;
+  return env != 0 && (Cout % 128 == 0 || (Cout % 64 == 0 && Cin_p >= 64));
 }
 
 // Choose the pixel box (Wb x Hb x Bb = P, powers of two) that wastes the
@@ -1340,13 +1268,14 @@ int make_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout, in
   g.TP = next_pow2(tc);
   g.BK = choose_bk((int)Cin_p, sparse);
   g.n_kc = (int)(Cin_p / g.BK);
-  if (use_tmode(Cout)) {
+  if (use_tmode(Cout, Cin_p)) {
     // N = 256 rows per tile unless that leaves a quarter of the SMs idle.
     g.tmode = 1;
-    g.BN = 128;
+    g.BN = Cout % 128 == 0 ? 128 : 64;
     g.NR = 256;
     choose_box(g.NR / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
-    if ((long)g.n_mtiles * (Cout / 128) < (148 * 3) / 4) {
+    static const int env_nr = getenv("CATFUSE_CONV_NR") ? atoi(getenv("CATFUSE_CONV_NR")) : 0;
+    if (env_nr == 128 || (env_nr != 256 && (long)g.n_mtiles * (Cout / g.BN) < (148 * 3) / 4)) {
       g.NR = 128;
       choose_box(g.NR / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
     }
@@ -1395,30 +1324,17 @@ int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, i
 template <int TP, int RES, bool FAST>
 int launch_t(const CUtensorMap& tmX, const CUtensorMap& tmW, ConvArgs args, int grid,
              cudaStream_t stream) {
-  const int w_bytes = 128 * args.BK * 2;
-  // 1 KB alignment slack, epilogue staging, up to 2*(8+8)+5 barriers + 2 words
-  const int fixed = 1024 + kTEpiWarps * kStageBytes + 512;
-  const int budget = kTSmemBudget - fixed;
-  int sa, sw;
-  if (args.khbox) {
-    sa = 2;
-    sw = (budget - sa * args.a_bytes) / w_bytes;
-  } else {
-    sa = sw = budget / (args.a_bytes + w_bytes);
-  }
-  if (sw > 8) sw = 8;
-  if (sa > 8) sa = 8;
-  if (args.stages > 1 && args.stages < sa) sa = args.stages;  // tuning override
-  if (sa < 2 || sw < 2) return fail(CF_ERR_UNSUPPORTED, "conv tile does not fit shared memory");
-  if (!args.khbox) sw = sa;
-  args.stages = sa;
-  args.wstages = sw;
+  const int stage_bytes = args.a_bytes + (args.khbox ? args.KH : 1) * args.MT * args.BK * 2;
+  const int fixed = kTFixedBytes;
+  int stages = (kTSmemBudget - fixed) / stage_bytes;
+  if (stages > 8) stages = 8;
+  if (args.stages > 1 && args.stages < stages) stages = args.stages;  // tuning override
+  if (stages < 2) return fail(CF_ERR_UNSUPPORTED, "conv tile does not fit shared memory");
+  args.stages = stages;
   // Round-robin producers may run at most one ring ahead only if there are
-  // no more of them than stages: kh-box mode has weight producers 1..3,
-  // paired mode producers 0..3.
-  if (args.khbox) args.nprod = sw < kProdWarps - 1 ? sw : kProdWarps - 1;
-  else args.nprod = sa < kProdWarps ? sa : kProdWarps;
-  int smem = fixed + sa * args.a_bytes + sw * w_bytes;
+  // no more of them than stages.
+  args.nprod = stages < kProdWarps ? stages : kProdWarps;
+  int smem = fixed + stages * stage_bytes;
   if (smem < 120 * 1024) smem = 120 * 1024;  // one TMEM-owning CTA per SM
   static bool attr_set = false;
   if (!attr_set) {
@@ -1536,8 +1452,12 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   const int fixed_bytes = 1024 + kEpiBytes + 256;
   static const int env_khbox = getenv("CATFUSE_CONV_KHBOX") ? atoi(getenv("CATFUSE_CONV_KHBOX")) : 1;
   // The kh shift (Wb*TP rows) must keep the operand on a 1 KB swizzle boundary.
+  // Two stages of (activation box + KH weight tiles) must fit beside the epilogue staging.
+  const int64_t khbox_stage = (int64_t)(g.Hb + KH - 1) * g.Wb * g.TP * g.BK * 2 +
+                              KH * (int64_t)g.BN * g.BK * 2;
   const int khbox = (g.tmode && env_khbox && stride == 1 && KH > 1 && g.Bb == 1 &&
-                     g.Hb + KH - 1 <= 256 && (g.Wb * g.TP * g.BK * 2) % 1024 == 0) ? 1 : 0;
+                     g.Hb + KH - 1 <= 256 && (g.Wb * g.TP * g.BK * 2) % 1024 == 0 &&
+                     2 * khbox_stage + kTFixedBytes <= kTSmemBudget) ? 1 : 0;
   const int halo = (!g.tmode && env_halo && wres && stride == 1 && g.Hb == 1 && g.Bb == 1 &&
                     g.Wb * g.TP == 128 && g.TP >= 4 && g.BK == 64 && Wh <= 256 && KH <= 256 &&
                     fixed_bytes + wslab + 2 * halo_bytes <= kSmemBudget) ? 1 : 0;
@@ -1595,7 +1515,8 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.lwb = __builtin_ctz((unsigned)g.Wb);
   args.lhb = __builtin_ctz((unsigned)g.Hb);
   if (g.tmode) {
-    args.idesc = make_idesc_f16(128, g.NR);
+    args.MT = g.BN;
+    args.idesc = make_idesc_f16(g.BN, g.NR);
     args.tmem_cols = (uint32_t)(2 * g.NR);
   } else {
     args.idesc = make_idesc_f16(128, g.BN);
@@ -1666,6 +1587,18 @@ int cf_conv_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout,
     return fail(CF_ERR_INVALID_ARG, "bad geometry query");
   Geometry g{};
   if (int rc = make_geometry(T, B, Ho, Wo, Cout, 64, 1, false, g)) return rc;
+  out6[0] = g.TP; out6[1] = g.Wb; out6[2] = g.Hb; out6[3] = g.Bb;
+  out6[4] = g.n_mtiles; out6[5] = g.BN;
+  return CF_OK;
+}
+
+int cf_conv_geometry_ex(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout,
+                        int64_t Cin_p, int64_t stride, int sparse, int32_t* out6) {
+  if (!out6 || T <= 0 || B <= 0 || Ho <= 0 || Wo <= 0 || Cout <= 0 || Cin_p <= 0 ||
+      Cin_p % 16 || stride <= 0)
+    return fail(CF_ERR_INVALID_ARG, "bad geometry query");
+  Geometry g{};
+  if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, sparse != 0, g)) return rc;
   out6[0] = g.TP; out6[1] = g.Wb; out6[2] = g.Hb; out6[3] = g.Bb;
   out6[4] = g.n_mtiles; out6[5] = g.BN;
   return CF_OK;

@@ -204,7 +204,8 @@ class NetworkPlan:
                 if st.lif is not None:
                     st.v = torch.zeros((b_, ho, wo, co), dtype=torch.float32, device=self.device)
                 if st.sparse:
-                    g = ops.conv_geometry(t_, b_, ho, wo, co)
+                    cin_p = self.shapes[st.src][-1]
+                    g = ops.conv_geometry(t_, b_, ho, wo, co, cin_p, st.stride, True)
                     st.mask = torch.zeros(g["n_mtiles"], dtype=torch.int32, device=self.device)
         self.fresh = True
         self._graphs = {}

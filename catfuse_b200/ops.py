@@ -275,10 +275,12 @@ def pack_conv_weight(w: torch.Tensor, Cin_p: Optional[int] = None):
 # fused conv / linear on tcgen05
 # ---------------------------------------------------------------------------
 
-def conv_geometry(T, B, Ho, Wo, Cout):
+def conv_geometry(T, B, Ho, Wo, Cout, Cin_p=64, stride=1, sparse=False):
+    """Tile geometry cf_conv_bn_lif uses for this output shape and input width
+    (the per-tile mask buffer of the sparse path has n_mtiles entries)."""
     import ctypes
     buf = (ctypes.c_int32 * 6)()
-    _lib.call("cf_conv_geometry", T, B, Ho, Wo, Cout, buf)
+    _lib.call("cf_conv_geometry_ex", T, B, Ho, Wo, Cout, Cin_p, stride, int(bool(sparse)), buf)
     return dict(TP=buf[0], Wb=buf[1], Hb=buf[2], Bb=buf[3], n_mtiles=buf[4], BN=buf[5])
 
 
@@ -378,7 +380,7 @@ def prescan_conv_tiles(x: torch.Tensor, Cout: int, KH: int, KW: int, stride: int
     B, H, W, T, Cin_p = x.shape
     Ho = (H + 2 * pad - KH) // stride + 1
     Wo = (W + 2 * pad - KW) // stride + 1
-    g = conv_geometry(T, B, Ho, Wo, Cout)
+    g = conv_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, True)
     chunk = conv_chunk(Cin_p, True)
     if mask_out is None:
         mask_out = torch.empty(g["n_mtiles"], dtype=torch.int32, device=x.device)

@@ -145,9 +145,14 @@ CF_API int cf_pack_conv_weight(const float* w, void* wp, int64_t Cout, int64_t C
 /* ---- fused Conv -> BN -> LIF on tcgen05 ----------------------------------- */
 
 /* Tile geometry of cf_conv_bn_lif for a shape; lets the caller size the
- * per-tile mask buffer.  out[0..5] = {Tp, Wb, Hb, Bb, n_mtiles, BN}. */
+ * per-tile mask buffer.  out[0..5] = {Tp, Wb, Hb, Bb, n_mtiles, BN}.
+ * cf_conv_geometry assumes Cin_p = 64, stride 1 and dense chunks; the tile
+ * choice depends on Cin_p, so callers that know it use cf_conv_geometry_ex
+ * (same output, the arguments cf_conv_bn_lif / cf_prescan_conv_tiles get). */
 CF_API int cf_conv_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo,
                      int64_t Cout, int32_t* out6);
+CF_API int cf_conv_geometry_ex(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout,
+                               int64_t Cin_p, int64_t stride, int sparse, int32_t* out6);
 
 /* Implicit-GEMM convolution on the 5th-generation tensor cores (fp16
  * operands, fp32 accumulation in TMEM) with the BN affine, the optional

@@ -165,7 +165,7 @@ def test_sparse_masks_and_bit_identity(dev, sparsity):
     nnz = torch.zeros(1, dtype=torch.int64, device=dev)
     mask = ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, nnz_out=nnz)
     assert int(nnz.item()) == int((x != 0).sum())
-    geom = ops.conv_geometry(T, B, H, W, C)
+    geom = ops.conv_geometry(T, B, H, W, C, xp.shape[-1], 1, True)
     chunk = ops.conv_chunk(xp.shape[-1], True)
     m_o = _conv_tile_mask_oracle(xp.cpu().numpy(), geom, 3, 3, 1, 1, chunk)
     assert np.array_equal(mask.cpu().numpy().astype(np.int64) & 0xFFFFFFFF, m_o)
