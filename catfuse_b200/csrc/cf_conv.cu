@@ -101,6 +101,7 @@ struct ConvArgs {
   int backoff;      // ns of sleep between polls for the non-critical waiters
   int tmode;        // 1: channel-major kernel (conv_t_kernel)
   int khbox;        // channel-major: one activation box covers all kh taps of a kw column
+  int kwgroup;      // channel-major: one stage carries the KW taps of a kernel row
   int NR;           // channel-major kernel: pixel x time rows per tile (MMA N)
   int MT;           // channel-major kernel: output channels per tile (MMA M), 128 or 64
   int lwb, lhb;     // log2 of Wb and Hb
@@ -860,15 +861,20 @@ __global__ void __launch_bounds__(kTThreads, 1)
   // column: tap (kh, kw) reads it from row kh*Wb*TP on, the step loop has
   // gh = 0 only and the stage holds KH weight tiles.  One barrier wait and one
   // commit then cover KH*BK/16 MMAs.
+  // kw-group mode (a.kwgroup, no kh-box): a stage carries the KW taps of one
+  // kernel row, each with its own activation box (XA bytes apart) and weight
+  // tile, and the step loop has gw = 0 only.
   const int n_gh = a.khbox ? 1 : a.KH;
-  const int nsub = a.khbox ? a.KH : 1;
+  const int n_gw = a.kwgroup ? 1 : a.KW;
+  const int nsub = a.khbox ? a.KH : (a.kwgroup ? a.KW : 1);
+  const int XSB = a.kwgroup ? nsub * XA : XA;  // activation bytes of one stage
   const int WSB = nsub * W_BYTES;    // weight bytes of one stage
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = smem;
-  uint8_t* sW = sX + (size_t)S * XA;
+  uint8_t* sW = sX + (size_t)S * XSB;
   uint8_t* sStage = sW + (size_t)S * WSB;  // epilogue staging, kStageBytes per warp
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStage + kTEpiWarps * kStageBytes);
   uint64_t* empty_bar = full_bar + S;
@@ -931,7 +937,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         const uint32_t km = tile_kmask(a, pt);
         if (km == 0) continue;
         for (int gh = 0; gh < n_gh && ok; ++gh) {
-          for (int gw = 0; gw < a.KW && ok; ++gw) {
+          for (int gw = 0; gw < n_gw && ok; ++gw) {
             for (int kc = 0; kc < a.n_kc; ++kc) {
               if (!((km >> kc) & 1u)) continue;
               const bool mine = owner == p;
@@ -952,11 +958,20 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 if (dbg & 1024) {
                   mbar_arrive(&full_bar[my_stage]);
                 } else {
-                  mbar_arrive_expect_tx(&full_bar[my_stage], XA + WSB);
-                  tma_load_5d(sX + (size_t)my_stage * XA, &tmX, &full_bar[my_stage], kc * BK,
-                              a.t0, wi0 + gw, hi0 + gh, b0);
+                  mbar_arrive_expect_tx(&full_bar[my_stage], XSB + WSB);
+                  if (a.kwgroup) {
+                    for (int j = 0; j < nsub; ++j)
+                      tma_load_5d(sX + (size_t)my_stage * XSB + (size_t)j * XA, &tmX,
+                                  &full_bar[my_stage], kc * BK, a.t0, wi0 + j, hi0 + gh, b0);
+                  } else {
+                    tma_load_5d(sX + (size_t)my_stage * XSB, &tmX, &full_bar[my_stage], kc * BK,
+                                a.t0, wi0 + gw, hi0 + gh, b0);
+                  }
+                  // sub-step j meets tap (gh + j, gw) in kh-box mode, (gh, j) in
+                  // kw-group mode, (gh, gw) otherwise
+                  const int tap_step = a.khbox ? a.KW : 1;
                   int tap = gh * a.KW + gw;
-                  for (int j = 0; j < nsub; ++j, tap += a.KW)
+                  for (int j = 0; j < nsub; ++j, tap += tap_step)
                     tma_load_2d(sW + (size_t)my_stage * WSB + (size_t)j * W_BYTES, &tmW,
                                 &full_bar[my_stage], tap * a.Cin_p + kc * BK, ct * MT);
                 }
@@ -979,10 +994,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t xa_step = (uint32_t)XA >> 4;
+      const uint32_t xa_step = (uint32_t)XSB >> 4;
       const uint32_t ws_step = (uint32_t)WSB >> 4;
       const uint32_t w_step = (uint32_t)W_BYTES >> 4;
-      const uint32_t sub_step = ((uint32_t)(a.Wb * TP) * ROWB) >> 4;  // kh-box row shift
+      // B operand advance per sub-step: kh-box row shift, or the next box
+      const uint32_t sub_step = a.kwgroup ? ((uint32_t)XA >> 4)
+                                          : (((uint32_t)(a.Wb * TP) * ROWB) >> 4);
       const uint64_t x_desc0 = make_smem_desc(smem_u32(sX), ROWB);
       const uint64_t w_desc0 = make_smem_desc(smem_u32(sW), ROWB);
       const int ksteps = BK / 16;
@@ -1010,7 +1027,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         } else {
           const uint32_t d_tmem = tmem_base + (uint32_t)(acc * NR);
           uint32_t accum = 0u;
-          const int n_g = n_gh * a.KW;
+          const int n_g = n_gh * n_gw;
           for (int g = 0; g < n_g && ok; ++g) {
             for (int kc = 0; kc < a.n_kc; ++kc) {
               if (!((km >> kc) & 1u)) continue;
@@ -1324,7 +1341,9 @@ int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, i
 template <int TP, int RES, bool FAST>
 int launch_t(const CUtensorMap& tmX, const CUtensorMap& tmW, ConvArgs args, int grid,
              cudaStream_t stream) {
-  const int stage_bytes = args.a_bytes + (args.khbox ? args.KH : 1) * args.MT * args.BK * 2;
+  const int nsub = args.khbox ? args.KH : (args.kwgroup ? args.KW : 1);
+  const int stage_bytes = (args.kwgroup ? nsub : 1) * args.a_bytes +
+                          nsub * args.MT * args.BK * 2;
   const int fixed = kTFixedBytes;
   int stages = (kTSmemBudget - fixed) / stage_bytes;
   if (stages > 8) stages = 8;
@@ -1535,6 +1554,15 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   static const int env_backoff = getenv("CATFUSE_CONV_BACKOFF") ? atoi(getenv("CATFUSE_CONV_BACKOFF")) : 256;
   args.backoff = env_backoff;
   args.khbox = khbox;
+  // Without a kh-box, group a kernel row's KW taps into one stage when two
+  // such stages fit: one barrier round trip per KW*BK/16 MMAs.
+  {
+    static const int env_kwg = getenv("CATFUSE_CONV_KWGROUP") ? atoi(getenv("CATFUSE_CONV_KWGROUP")) : 1;
+    const int64_t xa = (int64_t)g.NR * g.BK * 2;
+    const int64_t kwg_stage = KW * (xa + (int64_t)g.BN * g.BK * 2);
+    args.kwgroup = (g.tmode && !khbox && env_kwg && KW > 1 &&
+                    2 * kwg_stage + kTFixedBytes <= kTSmemBudget) ? 1 : 0;
+  }
   if (g.tmode)
     args.a_bytes = khbox ? (g.Hb + (int)KH - 1) * g.Wb * g.TP * g.BK * 2  // 1 KB multiple
                          : g.NR * g.BK * 2;
