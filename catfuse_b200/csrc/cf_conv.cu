@@ -152,13 +152,14 @@ __device__ __forceinline__ uint32_t tile_kmask(const ConvArgs& a, int mt) {
   return a.tile_mask ? (__ldg(a.tile_mask + mt) & a.kc_all) : a.kc_all;
 }
 
-// LIF step for the common configuration (decay_input, hard reset, tau a power
-// of two).  (z - (v - v_reset)) * (1/tau) is exact there, so the fused
-// multiply-add rounds exactly once, like the separately rounded form.
+// LIF step for the common configuration (decay_input, hard reset to 0, tau a
+// power of two).  With v_reset = 0, v - v_reset is v exactly and
+// (z - v) * (1/tau) is exact, so the fused multiply-add rounds exactly once,
+// like the separately rounded SpikingJelly form.
 __device__ __forceinline__ float lif_step_fast(float& v, float z, const LifParams& p) {
-  const float h = fmaf(__fsub_rn(z, __fsub_rn(v, p.v_reset)), p.rtau, v);
+  const float h = fmaf(__fsub_rn(z, v), p.rtau, v);
   const bool s = h >= p.v_th;
-  v = s ? p.v_reset : h;
+  v = s ? 0.0f : h;
   return s ? 1.0f : 0.0f;
 }
 
@@ -793,12 +794,16 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
         float z = fmaf(r[j], sc, sh);
         float o;
         if constexpr (RES == CF_RES_ADD_PRE) z = __fadd_rn(z, idv[j]);
+        __half oh;
         if constexpr (!kLif) {
           o = z;
+          oh = __float2half_rn(o);
         } else {
+          // a spike is 0 or 1: select its fp16 bits instead of converting
           o = lif_any<FAST>(vv, z, a.lp);
+          oh = __ushort_as_half(o != 0.f ? (unsigned short)0x3C00u : (unsigned short)0u);
         }
-        *reinterpret_cast<__half*>(hbase + stage_row_off<MT>(h * 32 + j)) = __float2half_rn(o);
+        *reinterpret_cast<__half*>(hbase + stage_row_off<MT>(h * 32 + j)) = oh;
       }
     }
     if (kLif) v[pp] = vv;
@@ -1542,7 +1547,8 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
     args.tmem_cols = (uint32_t)(2 * g.BN < 32 ? 32 : 2 * g.BN);
   }
   args.lp = make_lif(tau, v_th, v_reset, hard_reset, decay_input);
-  const bool fast = args.lp.decay_input && args.lp.hard_reset && args.lp.tau_pow2;
+  const bool fast = args.lp.decay_input && args.lp.hard_reset && args.lp.tau_pow2 &&
+                    args.lp.v_reset == 0.0f;
   // Tuning overrides for experiments: CATFUSE_CONV_STAGES, CATFUSE_CONV_DEBUG.
   static const int env_stages = getenv("CATFUSE_CONV_STAGES") ? atoi(getenv("CATFUSE_CONV_STAGES")) : 0;
   static const int env_debug = getenv("CATFUSE_CONV_DEBUG") ? atoi(getenv("CATFUSE_CONV_DEBUG")) : 0;
