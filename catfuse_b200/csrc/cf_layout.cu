@@ -189,17 +189,27 @@ __global__ void im2col_kernel(const void* __restrict__ x, int fmt, __half* __res
     const int ho = (int)(r % Ho);
     const int b = (int)(r / Ho);
     uint4* dst = reinterpret_cast<uint4*>(y + i * Kp);
+    // q = (kh*k + kw)*C + c walks with counters (no divisions per element)
+    const int64_t plane = (int64_t)H * W;
+    const int64_t base = ((int64_t)t * B + b) * C * plane;
+    const int ih0 = ho * s - p, iw0 = wo * s - p;
+    int c = 0, kw = 0, kh = 0;
     for (int q0 = 0; q0 < Kp; q0 += 8) {
       __align__(16) __half h[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int q = q0 + j;
         float v = 0.f;
-        if (q < KK) {
-          const int c = q % C, tap = q / C;
-          const int ih = ho * s - p + tap / k, iw = wo * s - p + tap % k;
+        if (q0 + j < KK) {
+          const int ih = ih0 + kh, iw = iw0 + kw;
           if (ih >= 0 && ih < H && iw >= 0 && iw < W)
-            v = ld_f(x, fmt, ((((int64_t)t * B + b) * C + c) * H + ih) * W + iw);
+            v = ld_f(x, fmt, base + c * plane + (int64_t)ih * W + iw);
+          if (++c == C) {
+            c = 0;
+            if (++kw == k) {
+              kw = 0;
+              ++kh;
+            }
+          }
         }
         h[j] = __float2half_rn(v);
       }

@@ -194,3 +194,23 @@ def test_conv_golden_reference(dev, golden_dir):
                      what="golden fp32 reference path")
     check_lif_parity(s, v, g["sf_spikes"], g["sf_vT"], h, v_tol=2e-2, near_tol=2e-2,
                      max_flip_rate=1e-4, what="golden StreamFuse kernel")
+
+
+@pytest.mark.parametrize("shape", [(4, 2, 3, 32, 32, 3, 1, 1, 32), (2, 3, 5, 9, 7, 3, 2, 1, 48),
+                                   (1, 2, 2, 6, 6, 5, 1, 2, 64)])
+def test_im2col_pack(dev, shape):
+    """Stem im2col pack: y[b,ho,wo,t,q] = x[t,b,c,ho*s-p+kh,wo*s-p+kw], q = (kh*k+kw)*C+c,
+    zero outside the image and for q >= k*k*C (exact: fp16 of the fp32 input)."""
+    ops = _ops()
+    T, B, C, H, W, k, s, p, Kp = shape
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(T, B, C, H, W, generator=g)
+    y = ops.pack_im2col(x.to(dev), k, s, p, Kp).cpu()
+    cols = torch.nn.functional.unfold(x.reshape(T * B, C, H, W), k, padding=p, stride=s)
+    Ho = (H + 2 * p - k) // s + 1
+    Wo = (W + 2 * p - k) // s + 1
+    # unfold rows are (c, kh, kw); the pack orders q as (kh, kw, c)
+    cols = cols.reshape(T, B, C, k * k, Ho, Wo).permute(1, 4, 5, 0, 3, 2).reshape(B, Ho, Wo, T, k * k * C)
+    ref = torch.zeros(B, Ho, Wo, T, Kp)
+    ref[..., :k * k * C] = cols
+    assert torch.equal(y, ref.half())
