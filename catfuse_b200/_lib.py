@@ -46,6 +46,8 @@ SIGNATURES = {
     "cf_unpack_bhwtc": (_INT, [_P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P]),
     "cf_v_layout": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _INT, _P]),
     "cf_pack_conv_weight": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
+    "cf_ssa_lif": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _F,
+                          _INT, _INT, _P]),
     "cf_conv_geometry": (_INT, [_I64, _I64, _I64, _I64, _I64, ctypes.POINTER(_I32)]),
     "cf_conv_geometry_ex": (_INT, [_I64, _I64, _I64, _I64, _I64, _I64, _I64, _INT,
                                    ctypes.POINTER(_I32)]),

@@ -2,6 +2,7 @@
 
     python -m catfuse_b200.conv_bench                      # config 0: T=4 B=32 128->128 32x32
     python -m catfuse_b200.conv_bench --shape 4,64,128,128,16,16,3,1,1 --reps 3
+    python -m catfuse_b200.conv_bench --ssa 4,64,64,384,12          # T,B,N,C,heads
 
 Shape = T,B,Cin,Cout,H,W,k,stride,pad.  Inputs are seeded Bernoulli(p) spikes and
 Kaiming-scaled weights; BN is the identity affine.  Each timed launch runs inside a
@@ -65,6 +66,38 @@ def run(shape, p=0.1, graph=20, reps=0, seed=0):
             "geometry": ops.conv_geometry(T, B, Ho, Wo, Co)}
 
 
+def run_ssa(shape, p=0.1, graph=20, seed=0):
+    """Time ops.ssa_lif (spiking self-attention + LIF) on seeded token spikes."""
+    T, B, N, C, heads = shape
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = ((torch.rand(B, N, T, C, generator=g) < p).half().to(dev) for _ in range(3))
+    out = torch.empty_like(q)
+    vo = torch.empty(B, N, C, device=dev)
+
+    def call():
+        ops.ssa_lif(q, k, v, heads, v_out=vo, out=out)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for _ in range(graph):
+            call()
+    gr.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    gr.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) / graph * 1e3
+    nbytes = 4 * B * N * T * C * 2 + B * N * C * 4
+    return {"shape": shape, "us": us, "gbs": nbytes / us / 1e3, "mb": nbytes / 1e6}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -73,7 +106,15 @@ def main(argv=None):
     ap.add_argument("--p", type=float, default=0.1, help="input spike probability")
     ap.add_argument("--graph", type=int, default=20, help="calls per timed graph")
     ap.add_argument("--reps", type=int, default=0, help="eager calls only, no timing")
+    ap.add_argument("--ssa", action="append", default=[],
+                    help="T,B,N,C,heads: time the spiking self-attention kernel instead")
     args = ap.parse_args(argv)
+    for sh in args.ssa:
+        r = run_ssa(tuple(int(v) for v in sh.split(",")), p=args.p, graph=args.graph)
+        print(f"ssa {r['shape']}: {r['us']:.1f} us, {r['gbs']:.0f} GB/s of algorithmic bytes "
+              f"({r['mb']:.1f} MB: q, k, v, spikes, v_T)")
+    if args.ssa and not args.shape:
+        return 0
     shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] or [CONFIG0]
     for shp in shapes:
         r = run(shp, p=args.p, graph=args.graph, reps=args.reps)

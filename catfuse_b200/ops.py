@@ -17,7 +17,7 @@ from ._lib import (FMT_BITS, FMT_F16, FMT_F32, FMT_U8, RES_ADD_POST, RES_ADD_PRE
                    RES_AND_POST, RES_IAND_POST, RES_NONE, RES_Z_ONLY, CatfuseNativeError)
 
 __all__ = [
-    "LIFConfig", "lif_fwd", "bn_lif", "add_lif", "avgpool_lif", "pack_tbchw", "unpack_bhwtc",
+    "LIFConfig", "ssa_lif", "lif_fwd", "bn_lif", "add_lif", "avgpool_lif", "pack_tbchw", "unpack_bhwtc",
     "v_to_nhwc", "v_to_nchw", "pack_im2col", "im2col_weight", "pack_conv_weight", "conv_bn_lif", "linear_bn_lif",
     "conv_geometry", "prescan", "prescan_conv_tiles", "conv_chunk", "avgpool_fc", "maxpool_bhwtc",
     "pad16", "SPIKE_FORMATS", "RES_MODES",
@@ -349,6 +349,26 @@ def linear_bn_lif(x: torch.Tensor, w: torch.Tensor, scale=None, shift=None, iden
               *lif.args(), _stream())
     return out
 
+
+
+def ssa_lif(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int,
+            scale: Optional[float] = None, v_in=None, v_out=None, lif: LIFConfig = _DEFAULT_LIF,
+            out=None):
+    """Spiking self-attention + attention LIF on token spikes q, k, v [B,N,T,C] fp16
+    (layout of linear_bn_lif) -> spikes [B,N,T,C] fp16; scale defaults to
+    head_dim ** -0.5; v_in / v_out [B,N,C] fp32 carry the attention LIF state."""
+    for t_, n_ in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t_, n_, torch.float16)
+    B, N, T, C = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k and v must have the same shape")
+    if scale is None:
+        scale = (C // heads) ** -0.5
+    if out is None:
+        out = torch.empty_like(q)
+    _lib.call("cf_ssa_lif", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+              _ptr(v_in), _ptr(v_out), T, B, N, C, heads, float(scale), *lif.args(), _stream())
+    return out
 
 # ---------------------------------------------------------------------------
 # prescan

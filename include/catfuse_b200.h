@@ -184,6 +184,19 @@ CF_API int cf_conv_bn_lif(const void* x, const void* wp, const float* scale,
                    int64_t pad, float tau, float v_threshold, float v_reset,
                    int hard_reset, int decay_input, void* stream);
 
+/* Spikformer spiking self-attention core + attention LIF: per head,
+ * y_t = (q_t k_t^T * scale) v_t, then the multi-step LIF over t.  q, k, v, out
+ * [B][N][T][C] fp16 spikes (the layout of cf_linear_bn_lif; any nonzero value
+ * is a spike), C = heads * head_dim, head_dim in {8,16,24,32}, N <= 64;
+ * v_in / v_out [B][N][C] fp32 (may be NULL; may alias).  Computed exactly as
+ * scale * (Q (K^T V)) in integers, one fp32 rounding per element.  Replaces
+ * the two matmuls and attn_lif of SSA.forward
+ * (models/spikformer_github.py:147-153). */
+CF_API int cf_ssa_lif(const void* q, const void* k, const void* v, void* out,
+                      const float* v_in, float* v_out, int64_t T, int64_t B, int64_t N,
+                      int64_t C, int64_t heads, float scale, float tau, float v_threshold,
+                      float v_reset, int hard_reset, int decay_input, void* stream);
+
 /* Linear -> (BN1d) -> LIF over tokens: x [B][L][T][Cin_p] fp16,
  * w [Cout][Cin_p] fp16, out [B][L][T][Cout] fp16.  A 1x1 convolution on the
  * same tensor-core kernel.  Replaces FusedLinearLIF

@@ -19,10 +19,11 @@ from .lif import lif_multistep, lif_multistep_triton_form
 from .bn import fold_bn
 from .conv import conv_bn_lif, conv_bn_lif_residual
 from .prescan import prescan_rf, choose_group_size, select_tile_sizes
+from .ssa import ssa_lif
 from .nets import sew_resnet18_forward, spiking_resnet18_forward, make_resnet18_params
 
 __all__ = [
     "lif_multistep", "lif_multistep_triton_form", "fold_bn", "conv_bn_lif",
     "conv_bn_lif_residual", "prescan_rf", "choose_group_size", "select_tile_sizes",
-    "sew_resnet18_forward", "spiking_resnet18_forward", "make_resnet18_params",
+    "sew_resnet18_forward", "spiking_resnet18_forward", "make_resnet18_params", "ssa_lif",
 ]

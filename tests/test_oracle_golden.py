@@ -70,3 +70,25 @@ def test_network_oracle_matches_sj_shim():
     functional.reset_net(net)
     with torch.no_grad():
         assert torch.equal(net(x), oracle.sew_resnet18_forward(x, p))
+
+
+def test_ssa_oracle_forms_agree():
+    """SSA restatement: the exact-integer form equals a per-head loop of the
+    reference's formula in float64, and the fp32 reference order stays within
+    a few ulp of it."""
+    import torch
+    g = torch.Generator().manual_seed(5)
+    T, B, N, C, heads = 2, 2, 12, 48, 3
+    q, k, v = ((torch.rand(T, B, N, C, generator=g) < 0.3).float().numpy() for _ in range(3))
+    _, _, y = oracle.ssa_lif(q, k, v, heads)
+    d = C // heads
+    sc = np.float32(d ** -0.5)
+    for t in range(T):
+        for b in range(B):
+            for h in range(heads):
+                sl = slice(h * d, (h + 1) * d)
+                ref = ((q[t, b, :, sl].astype(np.float64) @ k[t, b, :, sl].T.astype(np.float64))
+                       @ v[t, b, :, sl].astype(np.float64)) * np.float64(sc)
+                assert np.array_equal(y[t, b, :, sl], ref.astype(np.float32))
+    _, _, y_r = oracle.ssa_lif(q, k, v, heads, form="reference")
+    assert np.abs(y_r - y).max() <= 1e-5 * max(1.0, float(np.abs(y).max()))
