@@ -400,8 +400,9 @@ class FusedLinearLIF(CTFPattern):
         self.weight_io = nn.Parameter(torch.empty(in_features, out_features))
         nn.init.kaiming_normal_(self.weight_io.T)
         self.bias = None
-        self.bn_scale = None
-        self.bn_shift = None
+        # folded BN1d affine: buffers, so that .to(device) moves them with the weights
+        self.register_buffer("bn_scale", None)
+        self.register_buffer("bn_shift", None)
         self.state = StateBuffer()
         self._register_state(self.state)
 
@@ -699,6 +700,62 @@ class CTFSpikingBottleneck(CTFPattern):
         return cls(first, middle, last)
 
 
+class FusedSSA(CTFPattern):
+    """Spikformer spiking self-attention block over x[T, B, N, C]:
+    q/k/v = Linear->BN1d->LIF (fused tensor-core linear), the attention core
+    (q kᵀ · scale) v with its attention LIF in one kernel (``ops.ssa_lif``:
+    exact integer arithmetic on the spikes, membrane carried over T), then
+    proj = Linear->BN1d->LIF.  Mirrors SSA.forward of the reference
+    (models/spikformer_github.py:138-158); every LIF keeps its membrane in a
+    StateBuffer (StateCarry across calls) and ``reset()`` clears them all."""
+
+    policy_row = 4
+
+    def __init__(self, q, k, v, proj, heads: int, attn_tau: float = 2.0,
+                 attn_v_threshold: float = 1.0, attn_v_reset: Optional[float] = 0.0,
+                 scale: Optional[float] = None):
+        super().__init__()
+        self.q, self.k, self.v, self.proj = q, k, v, proj
+        self.heads = int(heads)
+        dim = q.out_features
+        if dim % self.heads:
+            raise ValueError("dim must be a multiple of heads")
+        self.scale = float((dim // self.heads) ** -0.5 if scale is None else scale)
+        self.attn_lif = ops.LIFConfig(tau=attn_tau, v_threshold=attn_v_threshold,
+                                      v_reset=attn_v_reset)
+        self.attn_state = StateBuffer()
+        self._register_state(self.attn_state)
+
+    def reset(self):
+        super().reset()
+        for m in (self.q, self.k, self.v, self.proj):
+            m.reset()
+
+    def forward(self, x):
+        if x.dim() != 4 or not x.is_cuda:
+            raise ValueError("FusedSSA expects a CUDA tensor x[T, B, N, C]")
+        T, B, N, C = x.shape
+        qs, ks, vs = self.q(x), self.k(x), self.v(x)          # [T, B, N, C] spikes
+        to_bntc = lambda s: s.permute(1, 2, 0, 3).to(torch.float16).contiguous()
+        v_att = self.attn_state.get((B, N, C), x.device)
+        y = ops.ssa_lif(to_bntc(qs), to_bntc(ks), to_bntc(vs), self.heads, self.scale,
+                        v_in=v_att, v_out=v_att, lif=self.attn_lif)
+        self.attn_state.set(v_att)
+        return self.proj(y.permute(2, 0, 1, 3).float())
+
+    @classmethod
+    def from_sj_modules(cls, sj_ssa):
+        """From a reference-style SSA module with q/q_bn/q_lif, k/..., v/...,
+        attn_lif, proj/proj_bn/proj_lif and num_heads."""
+        def lin(name):
+            return FusedLinearLIF.from_sj_modules(getattr(sj_ssa, name),
+                                                  getattr(sj_ssa, name + "_lif"),
+                                                  getattr(sj_ssa, name + "_bn", None))
+        tau, v_th, v_reset, _ = _lif_attrs(sj_ssa.attn_lif)
+        return cls(lin("q"), lin("k"), lin("v"), lin("proj"), sj_ssa.num_heads, tau, v_th,
+                   v_reset, getattr(sj_ssa, "scale", None))
+
+
 PATTERN_REGISTRY = {
     "PartialFusionConvLIF": PartialFusionConvLIF,
     "PartialFusionConvBNLIF": PartialFusionConvBNLIF,
@@ -712,6 +769,7 @@ PATTERN_REGISTRY = {
     "CTFSEWBottleneck": CTFSEWBottleneck,
     "CTFSpikingBottleneck": CTFSpikingBottleneck,
     "STFusionConvBNLIF": STFusionConvBNLIF,
+    "FusedSSA": FusedSSA,
 }
 
 __all__ = list(PATTERN_REGISTRY) + ["CTFPattern", "PATTERN_REGISTRY", "NativeConv"]
