@@ -91,6 +91,15 @@ class ClockSampler:
                  "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start: wait (bounded) for its first
+        # sample so that the timed region that follows is covered.
+        t_end = time.time() + 5.0
+        while time.time() < t_end and self.proc.poll() is None:
+            self.fh.flush()
+            if self.path.stat().st_size > 0:
+                break
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -162,17 +171,20 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    budget = max(2.0, min(20.0, 60.0 / max(args.steps + args.warmup, 1)))
-    for _ in range(args.warmup):
+    # At most 8 bounded CPU samples (~1 minute in total) whatever --steps asks:
+    # each step is a multi-second sample of the CPU workload, not one forward.
+    n_ref = max(1, min(args.steps, 8))
+    budget = max(2.0, min(20.0, 60.0 / (n_ref + min(args.warmup, 3))))
+    for _ in range(min(args.warmup, 3)):
         cpu_baseline(batch=8, budget_s=0.5)
-    vals = [cpu_baseline(batch=16, budget_s=budget) for _ in range(args.steps)]
+    vals = [cpu_baseline(batch=16, budget_s=budget) for _ in range(n_ref)]
     v = statistics.median(x["value"] for x in vals)
     base = vals[0]
     base["value"] = v
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * 16 / v, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference",
+            "impl": "reference", "cpu_samples": n_ref,
             "config": {"workload": "SEW-ResNet18 CIFAR T=4 forward (reference CPU path)",
                        "global_batch": 16, "seq_len": T_STEPS, "parallelism": "cpu"},
             "cpu_baseline": base,
@@ -184,7 +196,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch")
@@ -252,34 +264,44 @@ def main():
     ms_per_step = total_ms / args.steps
     value = world * B * args.steps / (total_ms / 1000.0)
 
-    # ---- kernel roofline: each conv launch timed alone with events ----------
+    # ---- kernel roofline: the forward's 20 conv launches replayed alone ------
+    # as one CUDA graph (same inputs, same order, L2 flushed before each
+    # replay), timed with events on the replaying stream.
     from catfuse_b200.network import ConvStep
     from catfuse_b200 import ops
-    conv_ms = []
-    for _ in range(3):
-        plan.fresh = True
-        ev = []
-        plan.pack_input()
+
+    def conv_launches():
         for st in plan.steps:
             if not isinstance(st, ConvStep):
                 continue
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            spec = st.native.spec
             ident = plan.acts[st.identity] if st.identity is not None else None
-            flush.fill_(1.0)
-            a.record()
             mode = "z_only" if st.lif is None else (st.res_mode if ident is not None else "none")
             ops.conv_bn_lif(plan.acts[st.src], st.wp, st.scale, st.shift, st.stride, st.pad,
                             identity=ident if st.lif is not None else None, res_mode=mode,
                             v_in=None, v_out=st.v, lif=st.lif or ops.LIFConfig(),
                             out=plan.acts[st.dst])
-            b.record()
-            ev.append((a, b))
+
+    plan.fresh = True
+    plan.pack_input()
+    conv_launches()                      # warm-up (also fills every activation)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    conv_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(conv_graph, stream=side):
+        conv_launches()
+    torch.cuda.synchronize()
+    conv_ms = []
+    for _ in range(5):
+        flush.fill_(1.0)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        conv_graph.replay()
+        b.record()
         torch.cuda.synchronize()
-        conv_ms.append(sum(a.elapsed_time(b) for a, b in ev))
+        conv_ms.append(a.elapsed_time(b))
     n_conv = sum(1 for st in plan.steps if isinstance(st, ConvStep))
-    conv_ms_fwd = min(conv_ms)
+    conv_ms_fwd = sum(conv_ms) / len(conv_ms)
     flops = _conv_flops(plan)
     peaks, peak_src = _peaks()
     achieved = flops / (conv_ms_fwd / 1000.0) / 1e12
@@ -287,7 +309,8 @@ def main():
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                 "traffic": traffic, "peak_source": f"{peak_src} bf16_tflops (burst)",
-                "kernel": "conv_bn_lif_kernel (all 20 conv launches of one forward)",
+                "kernel": "conv_t_kernel / conv_bn_lif_kernel (the 20 conv launches of one "
+                          "forward, replayed as one CUDA graph, L2 flushed before each replay)",
                 "flops_per_forward": flops, "conv_ms_per_forward": conv_ms_fwd,
                 "launches_per_forward": n_conv,
                 "share_of_step": conv_ms_fwd / ms_per_step}
