@@ -62,17 +62,39 @@ __global__ void __launch_bounds__(kPrescanThreads)
   uint32_t m = 0;
   const int64_t plane = (int64_t)H * W;
   const int64_t base = (int64_t)n * C * plane;
-  const int64_t total = (int64_t)C * rh * rw;
-  for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
-    const int col = (int)(e % rw);
-    const int row = (int)((e / rw) % rh);
-    const int c = (int)(e / ((int64_t)rw * rh));
-    const int ih = r0 + row, iw = c0 + col;
-    const int g = c / GS;
-    if ((m >> g) & 1u) continue;
-    if (!feeds(ih, o_h0, o_h1, k, s, p) || !feeds(iw, o_w0, o_w1, k, s, p)) continue;
-    const float v = load_any(x, fmt, base + c * plane + (int64_t)ih * W + iw);
-    if (fabsf(v) > thr) m |= 1u << g;
+  // Thread -> fixed receptive-field position (row, col), channels strided by
+  // the number of threads that share a position: divisions and the "does it
+  // feed an output of the tile" test run once per position, not per element.
+  const int P = rh * rw;
+  if (P > 0) {
+    // P <= blockDim: nrep threads share each position (channels strided by
+    // nrep); otherwise each thread walks positions tid, tid + blockDim, ...
+    const bool rep = (int)blockDim.x >= P;
+    const int nrep = rep ? (int)blockDim.x / P : 1;
+    const int pos_step = rep ? P : (int)blockDim.x;
+    const int tid = threadIdx.x;
+    if (tid < (rep ? nrep * P : (int)blockDim.x)) {
+      const int c_first = rep ? tid / P : 0;
+      for (int pos = rep ? tid % P : tid; pos < P; pos += pos_step) {
+        const int row = pos / rw, col = pos - (pos / rw) * rw;
+        const int ih = r0 + row, iw = c0 + col;
+        if (feeds(ih, o_h0, o_h1, k, s, p) && feeds(iw, o_w0, o_w1, k, s, p)) {
+          const int64_t off = base + (int64_t)ih * W + iw;
+          // four channels' loads in flight together, then the group bits
+          for (int c = c_first; c < C; c += 4 * nrep) {
+            float v4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int cu = c + u * nrep;
+              v4[u] = cu < C ? load_any(x, fmt, off + cu * plane) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (c + u * nrep < C && fabsf(v4[u]) > thr) m |= 1u << ((c + u * nrep) / GS);
+          }
+        }
+      }
+    }
   }
   // warp-level OR, then one shared atomic per warp
   for (int off = 16; off; off >>= 1) m |= __shfl_xor_sync(0xffffffffu, m, off);
@@ -94,7 +116,22 @@ __global__ void __launch_bounds__(kPrescanThreads)
   __syncthreads();
   unsigned long long c = 0;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+  const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t head = 0;
+  if (fmt == CF_FMT_F16 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    // 8 halves per 16-byte load; the scalar loop below takes the tail
+    const int64_t nv = n / 8;
+    const uint4* xv = static_cast<const uint4*>(x);
+    for (int64_t i = first; i < nv; i += stride) {
+      const uint4 u = __ldg(xv + i);
+      const uint32_t w4[4] = {u.x & 0x7FFF7FFFu, u.y & 0x7FFF7FFFu, u.z & 0x7FFF7FFFu,
+                              u.w & 0x7FFF7FFFu};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c += ((w4[j] & 0xFFFFu) != 0) + ((w4[j] >> 16) != 0);
+    }
+    head = nv * 8;
+  }
+  for (int64_t i = head + first; i < n; i += stride)
     c += (load_any(x, fmt, i) != 0.f) ? 1ull : 0ull;
   for (int off = 16; off; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
   if ((threadIdx.x & 31) == 0 && c) atomicAdd(&s_cnt, c);
@@ -134,34 +171,64 @@ __global__ void __launch_bounds__(kPrescanThreads)
     s_cnt = 0;
   }
   __syncthreads();
-  const int vec_per_pix = T * Cin_p / 8;
+  const int vec_per_pix = T * Cin_p / 8;  // 16-byte vectors per pixel
   const int rh = max(0, r1 - r0), rw = max(0, c1 - c0), nb = max(0, b1 - b0);
-  const int64_t total = (int64_t)nb * rh * rw * vec_per_pix;
+  const int npix = nb * rh * rw;
   uint32_t m = 0;
   unsigned long long cnt = 0;
-  for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
-    const int v = (int)(e % vec_per_pix);
-    const int64_t pix = e / vec_per_pix;
-    const int col = (int)(pix % rw);
-    const int row = (int)((pix / rw) % rh);
-    const int b = b0 + (int)(pix / ((int64_t)rw * rh));
-    const int ih = r0 + row, iw = c0 + col;
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(
-                              x + (((int64_t)b * H + ih) * W + iw) * (int64_t)T * Cin_p) +
-                          v);
-    const uint32_t w4[4] = {u.x & 0x7FFF7FFFu, u.y & 0x7FFF7FFFu, u.z & 0x7FFF7FFFu,
-                            u.w & 0x7FFF7FFFu};
-    const bool any = (w4[0] | w4[1] | w4[2] | w4[3]) != 0;
-    if (!any) continue;
-    const bool in_rf = ih >= rf_r0 && ih < rf_r1 && iw >= rf_c0 && iw < rf_c1;
-    if (in_rf) {
-      const int c = (v * 8) % Cin_p;
-      m |= 1u << (c / chunk);
-    }
-    if (count && ih >= own_r0 && ih < own_r1 && iw >= own_c0 && iw < own_c1) {
+  // Thread -> fixed vector slot v of a pixel (its channel chunk bit is then
+  // fixed too); pixels advance by a cursor (col, row, b), no divisions in the
+  // loop.  With more vectors per pixel than threads, each thread takes
+  // v = tid, tid + blockDim, ... of every pixel.
+  const int tid = threadIdx.x;
+  const bool rep = vec_per_pix <= (int)blockDim.x;
+  const int ppp = rep ? (int)blockDim.x / vec_per_pix : 1;  // pixels per pass
+  if (npix > 0 && (!rep || tid < ppp * vec_per_pix)) {
+    const int v0 = rep ? tid % vec_per_pix : tid;
+    int pix = rep ? tid / vec_per_pix : 0;
+    int col = pix % rw, row = (pix / rw) % rh, bb = pix / (rw * rh);
+    const int vstep = rep ? vec_per_pix : (int)blockDim.x;
+    constexpr int U = 4;  // pixels whose loads are in flight together
+    while (pix < npix) {
+      const uint4* px[U];
+      bool ok[U], in_rf[U], own[U];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        cnt += ((w4[j] & 0xFFFFu) != 0) + ((w4[j] >> 16) != 0);
+      for (int u = 0; u < U; ++u) {
+        ok[u] = pix < npix;
+        const int ih = r0 + row, iw = c0 + col;
+        px[u] = reinterpret_cast<const uint4*>(
+            x + (((int64_t)(b0 + bb) * H + ih) * W + iw) * (int64_t)T * Cin_p);
+        in_rf[u] = ih >= rf_r0 && ih < rf_r1 && iw >= rf_c0 && iw < rf_c1;
+        own[u] = count && ih >= own_r0 && ih < own_r1 && iw >= own_c0 && iw < own_c1;
+        // advance the cursor by ppp pixels
+        pix += ppp;
+        col += ppp;
+        while (col >= rw) {
+          col -= rw;
+          if (++row == rh) {
+            row = 0;
+            ++bb;
+          }
+        }
+      }
+      for (int v = v0; v < vec_per_pix; v += vstep) {
+        uint4 q[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) q[u] = ok[u] ? __ldg(px[u] + v) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t cbit = 1u << (((v * 8) % Cin_p) / chunk);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const uint32_t w4[4] = {q[u].x & 0x7FFF7FFFu, q[u].y & 0x7FFF7FFFu,
+                                  q[u].z & 0x7FFF7FFFu, q[u].w & 0x7FFF7FFFu};
+          if ((w4[0] | w4[1] | w4[2] | w4[3]) == 0) continue;
+          if (in_rf[u]) m |= cbit;
+          if (own[u]) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              cnt += ((w4[j] & 0xFFFFu) != 0) + ((w4[j] >> 16) != 0);
+          }
+        }
+      }
     }
   }
   for (int off = 16; off; off >>= 1) {

@@ -1,0 +1,127 @@
+"""Bandwidth benchmark of the memory-bound kernels at the BASELINE shapes.
+
+    python -m catfuse_b200.hbm_bench [--reps 10]
+
+Each call is timed alone with CUDA events, after a 256 MB write that evicts
+L2 (the write runs long enough for the host to queue the call behind it).
+Achieved bandwidth = algorithmic bytes / time; the peak is ``hbm_gbs`` of
+MEASURED_PEAKS.json when present (copy bandwidth measured on this pool).
+
+Cases (config numbers of BASELINE.json):
+* config 0 LIF family on z [T=4, B=32, 128, 32, 32]: lif_fwd (fp32 z -> fp16 /
+  u8 / bit-packed spikes), bn_lif, add_lif;
+* config 2 prescan over x [B=32, 28, 28, T=4, 256] fp16 (conv-tile masks) and
+  the reference-geometry prescan over the per-step NCHW view;
+* config 2 sparse conv sweep: Conv3x3-BN-LIF 256->256 at 28x28 with the
+  prescan masks, block sparsity s in {0.8, 0.9, 0.95, 0.99, 1.0}; bytes =
+  x read once + weights + spikes written + v_T, as a memory-bound kernel.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from . import ops
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _peak():
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _time(fn, reps, flush):
+    fn()
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(reps):
+        flush.fill_(1.0)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev) / reps * 1e3  # us
+
+
+def _block_sparse(T, B, C, H, W, s, g, dev):
+    nb = (T, B, C // 32, (H + 7) // 8, (W + 7) // 8)
+    keep = (torch.rand(nb, generator=g) >= s).float()
+    keep = keep.repeat_interleave(32, 2).repeat_interleave(8, 3).repeat_interleave(8, 4)[..., :H, :W]
+    return (keep * (torch.rand(T, B, C, H, W, generator=g) < 0.3).float()).to(dev)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--reps", type=int, default=10)
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    peak, src = _peak()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    g = torch.Generator().manual_seed(0)
+    rows = []
+
+    def report(name, us, nbytes):
+        gbs = nbytes / us / 1e3
+        rows.append((name, us, nbytes / 1e6, gbs, gbs / peak))
+        print(f"{name:58s} {us:8.1f} us {nbytes / 1e6:8.1f} MB {gbs:7.0f} GB/s "
+              f"{gbs / peak:6.1%} of {src} {peak:.0f}")
+
+    # ---- config 0: LIF family ---------------------------------------------
+    T, B, C, H, W = 4, 32, 128, 32, 32
+    N = B * C * H * W
+    z = (torch.randn(T, B, C, H, W, generator=g) * 0.8 + 0.3).to(dev)
+    for sd, sb, name in ((torch.float16, 2, "fp16"), (torch.uint8, 1, "u8"), ("bits", 1 / 8, "bits")):
+        us = _time(lambda: ops.lif_fwd(z, spike_dtype=sd), args.reps, flush)
+        report(f"lif_fwd  z fp32 -> spikes {name}  [4,32,128,32,32]", us, T * N * 4 + T * N * sb + 4 * N)
+    scale = torch.rand(C, generator=g).to(dev) + 0.5
+    shift = torch.randn(C, generator=g).to(dev) * 0.1
+    us = _time(lambda: ops.bn_lif(z, scale, shift, spike_dtype=torch.float16), args.reps, flush)
+    report("bn_lif   z fp32 -> spikes fp16", us, T * N * 4 + T * N * 2 + 4 * N + 8 * C)
+    z2 = torch.randn(T, B, C, H, W, generator=g).to(dev)
+    us = _time(lambda: ops.add_lif(z, z2, spike_dtype=torch.float16), args.reps, flush)
+    report("add_lif  2 x fp32 -> spikes fp16", us, T * N * 8 + T * N * 2 + 4 * N)
+
+    # ---- config 2: prescan and sparse conv sweep -----------------------------
+    T, B, C, H, W = 4, 32, 256, 28, 28
+    w = (torch.randn(C, C, 3, 3, generator=g) * (2.0 / (C * 9)) ** 0.5).to(dev)
+    sc = torch.ones(C, device=dev)
+    sh = torch.zeros(C, device=dev)
+    dense_us = None
+    for s in (0.8, 0.9, 0.95, 0.99, 1.0):
+        x = _block_sparse(T, B, C, H, W, s, g, dev)
+        xp = ops.pack_tbchw(x)
+        wp = ops.pack_conv_weight(w, xp.shape[-1])
+        xbytes = xp.numel() * 2
+        mask = ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1)
+        us = _time(lambda: ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, mask_out=mask), args.reps, flush)
+        report(f"prescan_conv_tiles  x [32,28,28,4,256] fp16  s={s}", us, xbytes + 4 * mask.numel())
+        v = torch.empty(B, H, W, C, device=dev)
+        out = torch.empty(B, H, W, T, C, dtype=torch.float16, device=dev)
+        conv_bytes = xbytes + wp.numel() * 2 + out.numel() * 2 + v.numel() * 4
+        if dense_us is None:
+            dense_us = _time(lambda: ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, v_out=v, out=out),
+                             args.reps, flush)
+            flops = 2.0 * T * B * H * W * C * C * 9
+            print(f"{'dense conv_bn_lif 256->256 28x28 (reference for the sweep)':58s} "
+                  f"{dense_us:8.1f} us  {flops / dense_us / 1e6:7.0f} TFLOP/s dense-equivalent")
+        us = _time(lambda: ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, v_out=v, out=out, tile_mask=mask),
+                   args.reps, flush)
+        report(f"sparse conv_bn_lif (masked) s={s}  [{us / dense_us:.2f}x dense time]", us, conv_bytes)
+    xr = x.reshape(T * B, C, H, W).half().contiguous()
+    us = _time(lambda: ops.prescan(xr, 3, 1, 1, 8, 8, 32), args.reps, flush)
+    report("prescan (reference geometry) x [128,256,28,28] fp16", us, xr.numel() * 2)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
