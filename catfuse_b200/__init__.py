@@ -12,7 +12,7 @@ __version__ = "0.1.0"
 
 
 def optimize(model, device="cuda:0", policy=None, T=16, use_sparseflow=True, native=True,
-             use_graph=True):
+             use_graph=True, precision="fp16"):
     """Rewrite ``model`` into fused CTF patterns.  Returns ``(model, stats)``.
 
     Reference: ``catfuse/__init__.py:9-13`` (there ``device`` and ``policy``
@@ -21,7 +21,10 @@ def optimize(model, device="cuda:0", policy=None, T=16, use_sparseflow=True, nat
     overriding the routing thresholds, and — for spiking ResNets — ``native``
     wraps the result in :class:`~catfuse_b200.network.CTFNetwork`, which runs
     the whole forward as one CUDA graph of fused kernels without leaving the
-    kernels' layout between layers.
+    kernels' layout between layers.  ``precision`` selects the conv operand
+    precision of the native plan: "fp16" (fp16 weights; spikes are exact) or
+    "split" (weights and the stem input as fp16 hi + lo pairs, fp32-faithful,
+    twice the tensor-core work).
     """
     import torch
     from .substitute import substitute, substitute_sf
@@ -35,7 +38,7 @@ def optimize(model, device="cuda:0", policy=None, T=16, use_sparseflow=True, nat
     if native:
         from .network import CTFNetwork, UnsupportedTopology
         try:
-            net = CTFNetwork(new_model, use_graph=use_graph)
+            net = CTFNetwork(new_model, use_graph=use_graph, precision=precision)
             stats["native_plan"] = True
             return net, stats
         except UnsupportedTopology as e:

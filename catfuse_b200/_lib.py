@@ -61,7 +61,14 @@ SIGNATURES = {
                                      _I64, _I64, _I64, _P]),
     "cf_conv_chunk": (_INT, [_I64, _INT]),
     "cf_maxpool_bhwtc": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
-    "cf_debug_read_trace": (_INT, [ctypes.POINTER(ctypes.c_longlong), _INT]),
+    "cf_conv_bn_lif_split": (_INT, [_P, _P, _P, _P, _P, _INT, _P, _P, _P, _P, _I64, _I64, _I64,
+                                    _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _INT,
+                                    _INT, _P]),
+    "cf_pack_conv_weight_split": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
+    "cf_pack_im2col_split": (_INT, [_P, _INT, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                    _I64, _P]),
+    "cf_set_wait_limit": (_INT, [ctypes.c_uint32]),
+    "cf_test_arm_stalled_load": (_INT, [_INT]),
     "cf_avgpool_fc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
 }
 

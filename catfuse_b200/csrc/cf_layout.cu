@@ -112,6 +112,31 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, __half* __restri
   }
 }
 
+// Split weights for the extended-precision conv: wp2[co][kh][kw][0][ci] =
+// hi = fp16(w * prescale), wp2[co][kh][kw][1][ci] = lo = fp16(w * prescale - hi).
+// prescale is a power of two, so w * prescale and the difference w*prescale - hi
+// are exact in fp32; hi + lo carries 22 significant bits of the weight.
+__global__ void pack_weight_split_kernel(const float* __restrict__ w, __half* __restrict__ wp,
+                                         int Cout, int Cin, int KH, int KW, int Cin_p,
+                                         float prescale) {
+  const int64_t n = (int64_t)Cout * KH * KW * Cin_p;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int ci = (int)(i % Cin_p);
+    const int64_t tap_row = i / Cin_p;  // (co, kh, kw)
+    int64_t r = tap_row;
+    const int kw = (int)(r % KW); r /= KW;
+    const int kh = (int)(r % KH);
+    const int co = (int)(r / KH);
+    float v = 0.f;
+    if (ci < Cin) v = __fmul_rn(w[(((int64_t)co * Cin + ci) * KH + kh) * KW + kw], prescale);
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+    wp[(tap_row * 2) * Cin_p + ci] = hi;
+    wp[(tap_row * 2 + 1) * Cin_p + ci] = lo;
+  }
+}
+
 // One CTA per (t, b): mean over H*W of x[b][:, :, t, :] into shared memory,
 // then one warp per class computes the fc dot product.
 __global__ void avgpool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
@@ -174,9 +199,12 @@ __global__ void maxpool_kernel(const __half* __restrict__ x, __half* __restrict_
 // im2col packing for a convolution with few input channels (the network stem):
 // y[b][ho][wo][t][q] = x[t][b][c][ho*s-p+kh][wo*s-p+kw] for q = (kh*k+kw)*C+c
 // (zero outside the image and for q >= k*k*C).
+// split = 1: y[..][q] = fp16(x) for q < k*k*C, and the rounding remainder
+// fp16(x - fp16(x)) of the same element at q + k*k*C (the stem's real-valued
+// input carried as hi + lo for the extended-precision conv).
 __global__ void im2col_kernel(const void* __restrict__ x, int fmt, __half* __restrict__ y, int T,
                               int B, int C, int H, int W, int Ho, int Wo, int k, int s, int p,
-                              int Kp) {
+                              int Kp, int split) {
   // One thread per output (pixel, t) row: gathers its k*k*C values and writes
   // the Kp-wide row with 16-byte stores.
   const int64_t n = (int64_t)B * Ho * Wo * T;
@@ -194,20 +222,23 @@ __global__ void im2col_kernel(const void* __restrict__ x, int fmt, __half* __res
     const int64_t base = ((int64_t)t * B + b) * C * plane;
     const int ih0 = ho * s - p, iw0 = wo * s - p;
     int c = 0, kw = 0, kh = 0;
+    const int qend = split ? 2 * KK : KK;
     for (int q0 = 0; q0 < Kp; q0 += 8) {
       __align__(16) __half h[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
+        const int q = q0 + j;
         float v = 0.f;
-        if (q0 + j < KK) {
+        if (q < qend) {
           const int ih = ih0 + kh, iw = iw0 + kw;
           if (ih >= 0 && ih < H && iw >= 0 && iw < W)
             v = ld_f(x, fmt, base + c * plane + (int64_t)ih * W + iw);
+          if (q >= KK) v = __fsub_rn(v, __half2float(__float2half_rn(v)));  // lo part
           if (++c == C) {
             c = 0;
             if (++kw == k) {
               kw = 0;
-              ++kh;
+              if (++kh == k) kh = 0;  // the lo pass restarts at tap (0, 0)
             }
           }
         }
@@ -295,13 +326,16 @@ int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b, float* lo
   return check_launch("avgpool_fc launch");
 }
 
-int cf_pack_im2col(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C, int64_t H,
-                   int64_t W, int64_t k, int64_t stride, int64_t pad, int64_t Kp, void* stream) {
+static int im2col_impl(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C,
+                       int64_t H, int64_t W, int64_t k, int64_t stride, int64_t pad, int64_t Kp,
+                       int split, void* stream) {
   if (!x || !y) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
   if (x_fmt != CF_FMT_F32 && x_fmt != CF_FMT_F16) return fail(CF_ERR_INVALID_ARG, "bad x_fmt");
+  const int64_t need = (split ? 2 : 1) * k * k * C;
   if (T <= 0 || B <= 0 || C <= 0 || H <= 0 || W <= 0 || k <= 0 || stride <= 0 || pad < 0 ||
-      Kp < k * k * C || Kp % 16)
-    return fail(CF_ERR_INVALID_ARG, "bad im2col shape (Kp >= k*k*C, Kp %% 16 == 0)");
+      Kp < need || Kp % 16)
+    return fail(CF_ERR_INVALID_ARG, "bad im2col shape (Kp >= %sk*k*C, Kp %% 16 == 0)",
+                split ? "2*" : "");
   const int64_t Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
   if (Ho <= 0 || Wo <= 0) return fail(CF_ERR_INVALID_ARG, "empty output map");
   if (int rc = require_sm100()) return rc;
@@ -312,8 +346,36 @@ int cf_pack_im2col(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int6
   if (blocks > 148 * 16) blocks = 148 * 16;
   im2col_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       x, x_fmt, static_cast<__half*>(y), (int)T, (int)B, (int)C, (int)H, (int)W, (int)Ho,
-      (int)Wo, (int)k, (int)stride, (int)pad, (int)Kp);
+      (int)Wo, (int)k, (int)stride, (int)pad, (int)Kp, split);
   return check_launch("im2col launch");
+}
+
+int cf_pack_im2col(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C, int64_t H,
+                   int64_t W, int64_t k, int64_t stride, int64_t pad, int64_t Kp, void* stream) {
+  return im2col_impl(x, x_fmt, y, T, B, C, H, W, k, stride, pad, Kp, 0, stream);
+}
+
+int cf_pack_im2col_split(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C,
+                         int64_t H, int64_t W, int64_t k, int64_t stride, int64_t pad, int64_t Kp,
+                         void* stream) {
+  return im2col_impl(x, x_fmt, y, T, B, C, H, W, k, stride, pad, Kp, 1, stream);
+}
+
+int cf_pack_conv_weight_split(const float* w, void* wp2, int64_t Cout, int64_t Cin, int64_t KH,
+                              int64_t KW, int64_t Cin_p, float prescale, void* stream) {
+  if (!w || !wp2) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (Cout <= 0 || Cin <= 0 || KH <= 0 || KW <= 0 || Cin_p < Cin || Cin_p % 16)
+    return fail(CF_ERR_INVALID_ARG, "bad weight shape (Cin_p >= Cin, Cin_p %% 16 == 0)");
+  int e = 0;
+  if (!(prescale > 0.f) || frexpf(prescale, &e) != 0.5f)
+    return fail(CF_ERR_INVALID_ARG, "prescale must be a positive power of two");
+  if (int rc = require_sm100()) return rc;
+  const int64_t n = Cout * KH * KW * Cin_p;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  pack_weight_split_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      w, static_cast<__half*>(wp2), (int)Cout, (int)Cin, (int)KH, (int)KW, (int)Cin_p, prescale);
+  return check_launch("pack_weight_split launch");
 }
 
 int cf_maxpool_bhwtc(const void* x, void* y, int64_t B, int64_t H, int64_t W, int64_t T,

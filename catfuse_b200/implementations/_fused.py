@@ -31,16 +31,26 @@ class _WeightCache:
         self.key = None
         self.wp = self.scale = self.shift = None
 
-    def get(self, spec: ConvLIFSpec, params: ConvLIFParams, device):
+    def get(self, spec: ConvLIFSpec, params: ConvLIFParams, device, precision: str = "fp16"):
+        """-> (packed weight, epilogue scale, epilogue shift) for ``precision``
+        ("fp16": wp[Cout,KH,KW,Cin_p]; "split": hi | lo weights with the
+        scale divided by their power-of-two prescale)."""
         def tag(t):
             return None if t is None else (id(t), t.data_ptr(), t._version, t.device)
-        key = (tag(params.weight), tag(params.bias), tag(params.bn_scale), tag(params.bn_bias), device)
+        key = (tag(params.weight), tag(params.bias), tag(params.bn_scale), tag(params.bn_bias),
+               device, precision)
         if key != self.key:
             w = params.weight.detach().to(device)
-            self.wp = ops.pack_conv_weight(w, ops.pad16(spec.in_channels))
             scale, shift = folded_affine(spec, params)
-            self.scale = None if scale is None else scale.to(device)
             self.shift = None if shift is None else shift.to(device)
+            if precision == "split":
+                self.wp, pre = ops.pack_conv_weight_split(w, ops.pad16(spec.in_channels))
+                base = (torch.ones(spec.out_channels, dtype=torch.float32, device=device)
+                        if scale is None else scale.to(device).float())
+                self.scale = (base / pre).contiguous()
+            else:
+                self.wp = ops.pack_conv_weight(w, ops.pad16(spec.in_channels))
+                self.scale = None if scale is None else scale.to(device)
             self.key = key
         return self.wp, self.scale, self.shift
 
@@ -56,14 +66,14 @@ def check_input(x: torch.Tensor, spec: ConvLIFSpec):
 
 def fused_forward(x: torch.Tensor, spec: ConvLIFSpec, params: ConvLIFParams, state,
                   cache: _WeightCache, sparse: bool, out_dtype=torch.float32,
-                  stats: Optional[dict] = None) -> torch.Tensor:
+                  stats: Optional[dict] = None, precision: str = "fp16") -> torch.Tensor:
     check_input(x, spec)
     T, B, Cin, H, W = x.shape
     Ho, Wo = spec.output_hw(H, W)
     Cout = spec.out_channels
     dev = x.device
-    wp, scale, shift = cache.get(spec, params, dev)
-    xp = ops.pack_tbchw(x.contiguous(), wp.shape[-1])
+    wp, scale, shift = cache.get(spec, params, dev, precision)
+    xp = ops.pack_tbchw(x.contiguous(), ops.pad16(spec.in_channels))
     v_in = state.get_native((B, Cout, Ho, Wo), dev)
     v_out = torch.empty((B, Ho, Wo, Cout), dtype=torch.float32, device=dev)
     mask = None
@@ -75,7 +85,7 @@ def fused_forward(x: torch.Tensor, spec: ConvLIFSpec, params: ConvLIFParams, sta
             stats["nnz"] = nnz
             stats["tile_mask"] = mask
     out = ops.conv_bn_lif(xp, wp, scale, shift, spec.stride, spec.padding, v_in=v_in,
-                          v_out=v_out, tile_mask=mask, lif=spec.lif_config())
+                          v_out=v_out, tile_mask=mask, lif=spec.lif_config(), precision=precision)
     state.set_native(v_out)
     return ops.unpack_bhwtc(out, dtype=out_dtype)
 

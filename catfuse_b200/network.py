@@ -115,7 +115,10 @@ class NetworkPlan:
     """Kernel launch list + static buffers for one input shape."""
 
     def __init__(self, model: nn.Module, T: int, B: int, H: int, W: int, device,
-                 use_sparse: bool = False):
+                 use_sparse: bool = False, precision: str = "fp16"):
+        if precision not in ops.PRECISIONS:
+            raise ValueError(f"precision must be one of {ops.PRECISIONS}")
+        self.precision = precision
         self.T, self.B, self.H, self.W = T, B, H, W
         self.device = torch.device(device)
         self.steps = []
@@ -128,10 +131,12 @@ class NetworkPlan:
         k0 = sspec.kernel_size
         # A stem with few input channels runs as a 1x1 convolution over an
         # im2col-packed input (one K chunk per tile instead of k*k taps).
-        self.im2col = k0 > 1 and cin * k0 * k0 <= 64
+        # (split precision: hi and lo parts of the real-valued input side by side)
+        kk_mult = 2 if precision == "split" else 1
+        self.im2col = k0 > 1 and kk_mult * cin * k0 * k0 <= 64
         if self.im2col:
             ho0, wo0 = sspec.output_hw(H, W)
-            self.shapes.append((B, ho0, wo0, T, ops.pad16(cin * k0 * k0)))
+            self.shapes.append((B, ho0, wo0, T, ops.pad16(kk_mult * cin * k0 * k0)))
         else:
             self.shapes.append((B, H, W, T, ops.pad16(cin)))
         self.stem_geom = (k0, sspec.stride, sspec.padding)
@@ -194,10 +199,17 @@ class NetworkPlan:
         self.acts = [torch.zeros(s, dtype=torch.float16, device=self.device) for s in self.shapes]
         for st in self.steps:
             if isinstance(st, ConvStep):
-                st.wp, st.scale, st.shift = st.native.packed(self.device)
+                st.wp, st.scale, st.shift = st.native.packed(self.device, precision)
                 if st.im2col:
-                    st.wp = ops.im2col_weight(st.native.params.weight.detach().to(self.device),
-                                              self.shapes[0][-1])
+                    w0 = st.native.params.weight.detach().to(self.device)
+                    if precision == "split":
+                        st.wp, pre = ops.im2col_weight_split(w0, self.shapes[0][-1])
+                        _, sc0, _ = st.native.packed(self.device, "fp16")
+                        base = (torch.ones(w0.shape[0], dtype=torch.float32, device=self.device)
+                                if sc0 is None else sc0.float())
+                        st.scale = (base / pre).contiguous()
+                    else:
+                        st.wp = ops.im2col_weight(w0, self.shapes[0][-1])
                 else:
                     st.stride, st.pad = st.native.spec.stride, st.native.spec.padding
                 b_, ho, wo, t_, co = self.shapes[st.dst]
@@ -220,7 +232,8 @@ class NetworkPlan:
     def pack_input(self):
         if self.im2col:
             k, s_, p_ = self.stem_geom
-            ops.pack_im2col(self.x_in, k, s_, p_, self.shapes[0][-1], out=self.acts[0])
+            pack = ops.pack_im2col_split if self.precision == "split" else ops.pack_im2col
+            pack(self.x_in, k, s_, p_, self.shapes[0][-1], out=self.acts[0])
         else:
             ops.pack_tbchw(self.x_in, self.shapes[0][-1], out=self.acts[0])
 
@@ -239,14 +252,15 @@ class NetworkPlan:
             ident = self.acts[st.identity] if st.identity is not None else None
             if st.lif is None:
                 ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
-                                st.pad, res_mode="z_only", out=self.acts[st.dst])
+                                st.pad, res_mode="z_only", out=self.acts[st.dst],
+                                precision=self.precision)
             else:
                 ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
                                 st.pad, identity=ident,
                                 res_mode=st.res_mode if ident is not None else "none",
                                 v_in=None if fresh else st.v, v_out=st.v,
                                 tile_mask=st.mask if st.sparse else None, lif=st.lif,
-                                out=self.acts[st.dst])
+                                out=self.acts[st.dst], precision=self.precision)
         ops.avgpool_fc(self.acts[self.final], self.fc_w, self.fc_b, out=self.logits)
 
     def run(self, use_graph: bool = True):
@@ -289,11 +303,15 @@ class CTFNetwork(nn.Module):
     """Wraps a rewritten spiking ResNet; ``forward(x[T, B, C, H, W])`` runs the
     native plan and returns logits [T, B, classes] (fp32)."""
 
-    def __init__(self, model: nn.Module, use_graph: bool = True, use_sparse: bool = False):
+    def __init__(self, model: nn.Module, use_graph: bool = True, use_sparse: bool = False,
+                 precision: str = "fp16"):
         super().__init__()
+        if precision not in ops.PRECISIONS:
+            raise ValueError(f"precision must be one of {ops.PRECISIONS}")
         self.model = model
         self.use_graph = use_graph
         self.use_sparse = use_sparse
+        self.precision = precision
         self._plans = {}
         self._fresh = True
         # validate now (raises UnsupportedTopology)
@@ -312,7 +330,7 @@ class CTFNetwork(nn.Module):
         key = (T, B, C, H, W, x.device)
         p = self._plans.get(key)
         if p is None:
-            p = NetworkPlan(self.model, T, B, H, W, x.device, self.use_sparse)
+            p = NetworkPlan(self.model, T, B, H, W, x.device, self.use_sparse, self.precision)
             self._plans[key] = p
         return p
 

@@ -20,8 +20,15 @@ __all__ = [
     "LIFConfig", "ssa_lif", "lif_fwd", "bn_lif", "add_lif", "avgpool_lif", "pack_tbchw", "unpack_bhwtc",
     "v_to_nhwc", "v_to_nchw", "pack_im2col", "im2col_weight", "pack_conv_weight", "conv_bn_lif", "linear_bn_lif",
     "conv_geometry", "prescan", "prescan_conv_tiles", "conv_chunk", "avgpool_fc", "maxpool_bhwtc",
-    "pad16", "SPIKE_FORMATS", "RES_MODES",
+    "pad16", "SPIKE_FORMATS", "RES_MODES", "PRECISIONS", "pack_conv_weight_split",
+    "pack_im2col_split", "im2col_weight_split", "split_prescale", "check_device_error",
+    "set_wait_limit",
 ]
+
+# Operand precision of the fused conv: "fp16" = fp16 weights (spikes are exact
+# in fp16); "split" = weights (and a real-valued stem input) carried as fp16
+# hi + lo parts, two MMAs per chunk into the same fp32 accumulator.
+PRECISIONS = ("fp16", "split")
 
 SPIKE_FORMATS = {torch.float32: FMT_F32, torch.float16: FMT_F16, torch.uint8: FMT_U8,
                  "bits": FMT_BITS}
@@ -260,6 +267,64 @@ def v_to_nchw(v: torch.Tensor, out: Optional[torch.Tensor] = None):
     return out
 
 
+def split_prescale(w: torch.Tensor) -> float:
+    """Power of two that brings max|w| to [2^13, 2^14): the lo parts of the
+    split weights then stay clear of the fp16 subnormal range."""
+    m = float(w.detach().abs().max()) if w.numel() else 0.0
+    if m == 0.0 or m != m:
+        return 1.0
+    import math
+    e = math.frexp(m)[1]  # m = f * 2^e, 0.5 <= f < 1
+    return float(2.0 ** (14 - e))
+
+
+def pack_conv_weight_split(w: torch.Tensor, Cin_p: Optional[int] = None,
+                           prescale: Optional[float] = None):
+    """w[Cout,Cin,KH,KW] -> (wp2[Cout,KH,KW,2*Cin_p] fp16 = hi | lo per tap, prescale).
+
+    The conv computes acc = x * (w * prescale); pass scale / prescale as the
+    epilogue scale (exact: prescale is a power of two)."""
+    w = w.detach().float().contiguous()
+    _need(w, "w", torch.float32)
+    Cout, Cin, KH, KW = w.shape
+    Cin_p = pad16(Cin) if Cin_p is None else int(Cin_p)
+    prescale = split_prescale(w) if prescale is None else float(prescale)
+    out = torch.empty((Cout, KH, KW, 2 * Cin_p), dtype=torch.float16, device=w.device)
+    _lib.call("cf_pack_conv_weight_split", w.data_ptr(), out.data_ptr(), Cout, Cin, KH, KW, Cin_p,
+              prescale, _stream())
+    return out, prescale
+
+
+def pack_im2col_split(x: torch.Tensor, k: int, stride: int, pad: int, Kp: Optional[int] = None,
+                      out: Optional[torch.Tensor] = None):
+    """x[T,B,C,H,W] -> [B,Ho,Wo,T,Kp] fp16 with hi parts at q < k*k*C and the
+    rounding remainders (lo) at q + k*k*C."""
+    _need(x, "x")
+    T, B, C, H, W = x.shape
+    Kp = pad16(2 * k * k * C) if Kp is None else int(Kp)
+    Ho = (H + 2 * pad - k) // stride + 1
+    Wo = (W + 2 * pad - k) // stride + 1
+    if out is None:
+        out = torch.empty((B, Ho, Wo, T, Kp), dtype=torch.float16, device=x.device)
+    _lib.call("cf_pack_im2col_split", x.data_ptr(), _zfmt(x), out.data_ptr(), T, B, C, H, W, k,
+              stride, pad, Kp, _stream())
+    return out
+
+
+def im2col_weight_split(w: torch.Tensor, Kp: Optional[int] = None):
+    """Weights for pack_im2col_split inputs: the row [w, w, 0...] (hi and lo
+    input parts both meet the full weight), split into hi | lo.
+    -> (wp2[Cout,1,1,2*Kp] fp16, prescale)."""
+    Cout, Cin, kh, kw = w.shape
+    KK = kh * kw * Cin
+    Kp = pad16(2 * KK) if Kp is None else int(Kp)
+    flat = w.detach().float().permute(0, 2, 3, 1).reshape(Cout, KK)
+    row = torch.zeros((Cout, Kp), dtype=torch.float32, device=w.device)
+    row[:, :KK] = flat
+    row[:, KK:2 * KK] = flat
+    return pack_conv_weight_split(row.reshape(Cout, Kp, 1, 1), Kp)
+
+
 def pack_conv_weight(w: torch.Tensor, Cin_p: Optional[int] = None):
     """w[Cout,Cin,KH,KW] -> [Cout,KH,KW,Cin_p] fp16 (zero padded)."""
     w = w.detach().float().contiguous()
@@ -296,17 +361,23 @@ def conv_bn_lif(x: torch.Tensor, wp: torch.Tensor, scale: Optional[torch.Tensor]
                 identity: Optional[torch.Tensor] = None, res_mode=None,
                 v_in: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None,
                 tile_mask: Optional[torch.Tensor] = None, lif: LIFConfig = _DEFAULT_LIF,
-                out: Optional[torch.Tensor] = None):
-    """Fused conv+BN+LIF on x[B,H,W,T,Cin_p] fp16 with wp[Cout,KH,KW,Cin_p] fp16.
+                out: Optional[torch.Tensor] = None, precision: str = "fp16"):
+    """Fused conv+BN+LIF on x[B,H,W,T,Cin_p] fp16 with wp[Cout,KH,KW,Cin_p] fp16
+    (precision "fp16") or split weights wp[Cout,KH,KW,2*Cin_p] from
+    pack_conv_weight_split (precision "split"; scale already divided by the
+    prescale).
 
     Returns out[B,Ho,Wo,T,Cout] fp16.  v_out (if given) receives v_T in
     [B,Ho,Wo,Cout] fp32; v_in may alias v_out."""
     _need(x, "x", torch.float16)
     _need(wp, "wp", torch.float16)
+    if precision not in PRECISIONS:
+        raise ValueError(f"precision must be one of {PRECISIONS}")
     B, H, W, T, Cin_p = x.shape
     Cout, KH, KW, Cw = wp.shape
-    if Cw != Cin_p:
-        raise ValueError(f"weight Cin_p {Cw} != activation Cin_p {Cin_p}")
+    if Cw != (2 if precision == "split" else 1) * Cin_p:
+        raise ValueError(f"weight channels {Cw} do not match activation Cin_p {Cin_p} "
+                         f"at precision {precision!r}")
     Ho = (H + 2 * pad - KH) // stride + 1
     Wo = (W + 2 * pad - KW) // stride + 1
     mode = RES_MODES[res_mode] if not isinstance(res_mode, int) else res_mode
@@ -328,7 +399,8 @@ def conv_bn_lif(x: torch.Tensor, wp: torch.Tensor, scale: Optional[torch.Tensor]
         out = torch.empty((B, Ho, Wo, T, Cout), dtype=torch.float16, device=x.device)
     else:
         _need(out, "out", torch.float16)
-    _lib.call("cf_conv_bn_lif", x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
+    fn = "cf_conv_bn_lif_split" if precision == "split" else "cf_conv_bn_lif"
+    _lib.call(fn, x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
               _ptr(identity), mode, _ptr(v_in), _ptr(v_out), out.data_ptr(), _ptr(tile_mask),
               T, B, H, W, Cin_p, Cout, KH, KW, stride, pad, *lif.args(), _stream())
     return out
@@ -437,3 +509,24 @@ def avgpool_fc(x: torch.Tensor, fc_w: torch.Tensor, fc_b: Optional[torch.Tensor]
     _lib.call("cf_avgpool_fc", x.data_ptr(), fc_w.data_ptr(), _ptr(fc_b), out.data_ptr(), T, B, H,
               W, C, K, _stream())
     return out
+
+
+# ---------------------------------------------------------------------------
+# bounded device-side waits
+# ---------------------------------------------------------------------------
+
+def check_device_error(stream: Optional[int] = None) -> None:
+    """Raise CatfuseNativeError(CF_ERR_DEVICE_TIMEOUT) if a bounded wait inside
+    a fused conv launch expired since the last check (synchronises the stream;
+    the error word is cleared by the read)."""
+    import ctypes
+    code = ctypes.c_int32(0)
+    rc = _lib.load().cf_check_device_error(_stream() if stream is None else stream,
+                                           ctypes.byref(code))
+    _lib.check(rc, f"device-side wait expired (site {code.value})")
+
+
+def set_wait_limit(max_polls: int = 0) -> None:
+    """Bound on the polls of every device-side wait of later conv launches
+    (0 restores the default of 2^24 polls)."""
+    _lib.call("cf_set_wait_limit", int(max_polls))

@@ -60,9 +60,10 @@ class NativeConv:
         self.spec = spec
         self.params = params
 
-    def packed(self, device):
-        cache = self.owner.__dict__.setdefault("_native_cache", _WeightCache())
-        return cache.get(self.spec, self.params, device)
+    def packed(self, device, precision: str = "fp16"):
+        caches = self.owner.__dict__.setdefault("_native_caches", {})
+        cache = caches.setdefault(precision, _WeightCache())
+        return cache.get(self.spec, self.params, device, precision)
 
 
 class CTFPattern(*_BASES):

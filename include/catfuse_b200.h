@@ -245,9 +245,52 @@ CF_API int cf_maxpool_bhwtc(const void* x, void* y, int64_t B, int64_t H, int64_
                             int64_t T, int64_t C, int64_t k, int64_t stride, int64_t pad,
                             void* stream);
 
-/* Tuning aid: copies n (<= 1024) clock64 stamps recorded by the fused conv
- * kernel when CATFUSE_CONV_DEBUG has bit 8 set (synchronous). */
-CF_API int cf_debug_read_trace(long long* host, int n);
+/* Extended-precision variant of cf_conv_bn_lif: the weight is carried as two
+ * fp16 parts, wp2[Cout][KH][KW][2][Cin_p] = {hi, lo} (cf_pack_conv_weight_split),
+ * and every (tap, channel chunk) issues the hi and the lo MMAs into the same
+ * fp32 TMEM accumulator, so the conv sums x * (hi + lo) with 22 significant
+ * weight bits (fp32-faithful for spike inputs, which fp16 holds exactly; a
+ * real-valued stem input is split the same way by cf_pack_im2col_split).
+ * Twice the MMA work of cf_conv_bn_lif; same arguments otherwise, with `scale`
+ * already divided by the prescale the weights were packed with.  Serves the
+ * fp32 reference path of DenseKeep (catfuse/implementations/dense_keep.py:97-155,
+ * cuDNN fp32 conv) where fp16 weight rounding is not acceptable. */
+CF_API int cf_conv_bn_lif_split(const void* x, const void* wp2, const float* scale,
+                                const float* shift, const void* identity, int res_mode,
+                                const float* v_in, float* v_out, void* out,
+                                const uint32_t* tile_mask,
+                                int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin_p,
+                                int64_t Cout, int64_t KH, int64_t KW, int64_t stride,
+                                int64_t pad, float tau, float v_threshold, float v_reset,
+                                int hard_reset, int decay_input, void* stream);
+/* w[Cout][Cin][KH][KW] fp32 -> wp2[Cout][KH][KW][2][Cin_p] fp16 with
+ * hi = fp16(w * prescale) and lo = fp16(w * prescale - hi); prescale is a
+ * power of two (chosen so that the largest |w * prescale| is near 2^14 and lo
+ * stays out of the fp16 subnormal range). */
+CF_API int cf_pack_conv_weight_split(const float* w, void* wp2, int64_t Cout, int64_t Cin,
+                                     int64_t KH, int64_t KW, int64_t Cin_p, float prescale,
+                                     void* stream);
+/* cf_pack_im2col for the extended-precision stem: y[..][q] = fp16(v) for
+ * q < k*k*C and fp16(v - fp16(v)) of the same element at q + k*k*C
+ * (Kp >= 2*k*k*C).  With the weight row [w, w] this gives x*w with both
+ * operands carried as hi + lo. */
+CF_API int cf_pack_im2col_split(const void* x, int x_fmt, void* y, int64_t T, int64_t B,
+                                int64_t C, int64_t H, int64_t W, int64_t k, int64_t stride,
+                                int64_t pad, int64_t Kp, void* stream);
+
+/* ---- bounded device-side waits ------------------------------------------- */
+
+/* Every mbarrier wait inside the fused conv kernel gives up after a bounded
+ * number of polls, records a site code in the device error word
+ * (cf_check_device_error) and ends the kernel early.  This sets that bound for
+ * later launches in this process (0 = the default, 2^24 polls, i.e. seconds).
+ * The reference has no counterpart (Triton kernels there have no waits). */
+CF_API int cf_set_wait_limit(uint32_t max_polls);
+/* Test hook for that expiry path: when armed, the next cf_conv_bn_lif launch
+ * has CTA 0's producers skip their first load, so the consumer's wait for it
+ * runs out; the kernel ends early and cf_check_device_error reports
+ * CF_ERR_DEVICE_TIMEOUT.  One-shot (disarmed by that launch); 0 disarms. */
+CF_API int cf_test_arm_stalled_load(int armed);
 
 /* ---- network head ---------------------------------------------------------- */
 

@@ -79,8 +79,9 @@ def make_resnet18_params(num_classes=10, stem="cifar", seed=0, in_ch=3):
     return p
 
 
-def _resnet18_forward(x, p, sew, stem, record=None, branch_dtype=None):
-    x = torch.as_tensor(x, dtype=torch.float32)
+def _resnet18_forward(x, p, sew, stem, record=None, branch_dtype=None, dtype=torch.float32):
+    x = torch.as_tensor(x).to(dtype)
+    p = {k: (v.to(dtype) if torch.is_floating_point(v) else v) for k, v in p.items()}
     if stem == "cifar":
         z = _conv_bn(x, p, "conv1", "bn1", 1, 1)
     else:
@@ -131,9 +132,10 @@ def _resnet18_forward(x, p, sew, stem, record=None, branch_dtype=None):
     return F.linear(pooled, p["fc.weight"], p["fc.bias"])  # [T, B, K]
 
 
-def sew_resnet18_forward(x, p, stem="cifar", record=None):
-    """x: [T, B, 3, H, W] -> logits [T, B, K]."""
-    return _resnet18_forward(x, p, True, stem, record)
+def sew_resnet18_forward(x, p, stem="cifar", record=None, dtype=torch.float32):
+    """x: [T, B, 3, H, W] -> logits [T, B, K].  ``dtype`` float64 gives the
+    high-precision reference against which fp32 paths are measured."""
+    return _resnet18_forward(x, p, True, stem, record, None, dtype)
 
 
 def spiking_resnet18_forward(x, p, stem="imagenet", record=None, branch_dtype=None):

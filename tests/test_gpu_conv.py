@@ -6,6 +6,7 @@ import pytest
 import torch
 
 import oracle
+from catfuse_b200 import workloads
 from lif_parity import check_lif_parity, lif_trace
 
 pytestmark = pytest.mark.gpu
@@ -25,12 +26,17 @@ def _case(T, B, Cin, Cout, H, W, k, seed, p=0.25):
     return x, w, scale, shift
 
 
-def _run(dev, x, w, scale, shift, stride, pad, **kw):
+def _run(dev, x, w, scale, shift, stride, pad, precision="fp16", **kw):
     ops = _ops()
     T, B, Cin, H, W = x.shape
     Cout = w.shape[0]
     xp = ops.pack_tbchw(x.to(dev))
-    wp = ops.pack_conv_weight(w.to(dev), xp.shape[-1])
+    if precision == "split":
+        wp, pre = ops.pack_conv_weight_split(w.to(dev), xp.shape[-1])
+        scale = scale / pre
+        kw["precision"] = "split"
+    else:
+        wp = ops.pack_conv_weight(w.to(dev), xp.shape[-1])
     Ho = (H + 2 * pad - w.shape[2]) // stride + 1
     Wo = (W + 2 * pad - w.shape[3]) // stride + 1
     v_out = torch.empty(B, Ho, Wo, Cout, device=dev)
@@ -149,17 +155,17 @@ def _conv_tile_mask_oracle(x_bhwtc, geom, KH, KW, st, pad, chunk):
     return np.array(masks, dtype=np.int64)
 
 
-@pytest.mark.parametrize("sparsity", [0.8, 0.95, 1.0])
+@pytest.mark.parametrize("sparsity", workloads.CONFIG2["sparsities"])
 def test_sparse_masks_and_bit_identity(dev, sparsity):
-    """SparseFlow: prescan masks are exact; masked conv == dense conv bit for bit."""
+    """SparseFlow at the config-2 shape ([4, 32, 256, 28, 28], 8x8x32 zero
+    blocks): the conv-tile prescan masks are exact, the masked conv matches
+    the oracle, and it is bit-identical to the unmasked launch of the same
+    geometry (every chunk enabled) -- skipped chunks add exact zeros."""
     ops = _ops()
-    T, B, C, H, W = 4, 4, 256, 14, 14
-    g = torch.Generator().manual_seed(31)
-    nb = (T, B, C // 32, (H + 7) // 8, (W + 7) // 8)
-    keep = (torch.rand(nb, generator=g) >= sparsity).float()
-    keep = keep.repeat_interleave(32, 2).repeat_interleave(8, 3).repeat_interleave(8, 4)[..., :H, :W]
-    x = keep * (torch.rand(T, B, C, H, W, generator=g) < 0.3).float()
-    _, w, scale, shift = _case(T, B, C, C, H, W, 3, seed=32)
+    c = workloads.CONFIG2
+    T, B, C, H, W = c["T"], c["B"], c["C"], c["H"], c["W"]
+    x = workloads.block_sparse_spikes(T, B, C, H, W, sparsity, seed=31)
+    _, w, scale, shift = _case(1, 1, C, C, 1, 1, 3, seed=32)
     xp = ops.pack_tbchw(x.to(dev))
     wp = ops.pack_conv_weight(w.to(dev), xp.shape[-1])
     nnz = torch.zeros(1, dtype=torch.int64, device=dev)
@@ -169,15 +175,98 @@ def test_sparse_masks_and_bit_identity(dev, sparsity):
     chunk = ops.conv_chunk(xp.shape[-1], True)
     m_o = _conv_tile_mask_oracle(xp.cpu().numpy(), geom, 3, 3, 1, 1, chunk)
     assert np.array_equal(mask.cpu().numpy().astype(np.int64) & 0xFFFFFFFF, m_o)
-    dense = ops.conv_bn_lif(xp, wp, scale.to(dev), shift.to(dev), 1, 1)
-    sparse = ops.conv_bn_lif(xp, wp, scale.to(dev), shift.to(dev), 1, 1, tile_mask=mask)
-    # skipped chunks add exact zeros; the same BK is used when the mask is
-    # absent only if chunk == dense BK, so compare against the oracle too
+    sc, sh = scale.to(dev), shift.to(dev)
+    sparse = ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, tile_mask=mask)
+    full = torch.full_like(mask, -1)  # every chunk of every tile: same geometry, no skipping
+    unmasked = ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, tile_mask=full)
+    torch.cuda.synchronize()
+    assert torch.equal(sparse, unmasked)
     s_o, _ = oracle.conv_bn_lif(x, w, scale, shift, 1, 1, operand_dtype=torch.float16)
     sp = ops.unpack_bhwtc(sparse).cpu().numpy()
     assert (sp != s_o).mean() <= 1e-4
-    if chunk == ops.conv_chunk(xp.shape[-1], False):
-        assert torch.equal(dense, sparse)
+    if sparsity == 1.0:
+        # StaticZero: z = shift everywhere
+        s_z, _ = oracle.conv_bn_lif(torch.zeros_like(x), w, scale, shift, 1, 1)
+        assert np.array_equal(sp, s_z)
+
+
+def test_config0_exact(dev):
+    """Config 0 exactly: T=4, B=32, 128->128, 32x32, Bernoulli(0.1) spikes,
+    Kaiming weights, BN statistics of the stated distributions."""
+    x, w, scale, shift = workloads.config0()
+    s, v, _ = _run(dev, x, w, scale, shift, 1, 1)
+    s_o, v_o, z = oracle.conv_bn_lif(x, w, scale, shift, 1, 1, operand_dtype=torch.float16,
+                                     return_z=True)
+    _, _, h = lif_trace(z)
+    check_lif_parity(s, v, s_o, v_o, h, v_tol=1e-4, near_tol=1e-3, max_flip_rate=1e-4,
+                     what="config 0, fp16-operand oracle")
+    s32, v32, z32 = oracle.conv_bn_lif(x, w, scale, shift, 1, 1, return_z=True)
+    _, _, h32 = lif_trace(z32)
+    check_lif_parity(s, v, s32, v32, h32, v_tol=2e-2, near_tol=2e-2, max_flip_rate=1e-4,
+                     what="config 0, fp32 oracle")
+    # the extended-precision (split-weight) path meets the fp32 tolerance
+    ss, vs, _ = _run(dev, x, w, scale, shift, 1, 1, precision="split")
+    check_lif_parity(ss, vs, s32, v32, h32, v_tol=1e-4, near_tol=1e-4, max_flip_rate=1e-4,
+                     what="config 0, split precision vs fp32 oracle")
+    assert s32.mean() > 1e-3
+
+
+SPLIT_SHAPES = [
+    (4, 2, 64, 64, 8, 8, 3, 1, 1),          # pixel-major kernel
+    (4, 2, 64, 32, 32, 32, 3, 1, 1),        # pixel-major, resident weights, halo box
+    (4, 4, 128, 128, 16, 16, 3, 1, 1),      # channel-major, kh-box
+    (4, 2, 64, 128, 16, 16, 3, 2, 1),       # channel-major, stride 2
+    (4, 2, 64, 128, 16, 16, 1, 2, 0),       # 1x1 downsample
+    (4, 2, 512, 512, 4, 4, 3, 1, 1),        # kw-group stages
+    (12, 1, 32, 128, 5, 5, 3, 1, 1),        # chunked T
+]
+
+
+@pytest.mark.parametrize("shape", SPLIT_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_split_precision_vs_fp32(dev, shape):
+    """Split (hi + lo) weights: fp32-faithful -- v within 1e-4 of the fp32
+    oracle and flips only within 1e-4 of the threshold."""
+    T, B, Cin, Cout, H, W, k, st, pad = shape
+    x, w, scale, shift = _case(T, B, Cin, Cout, H, W, k, seed=hash(shape) % 997)
+    s, v, _ = _run(dev, x, w, scale, shift, st, pad, precision="split")
+    s32, v32, z32 = oracle.conv_bn_lif(x, w, scale, shift, st, pad, return_z=True)
+    _, _, h32 = lif_trace(z32)
+    check_lif_parity(s, v, s32, v32, h32, v_tol=1e-4, near_tol=1e-4, max_flip_rate=1e-4,
+                     what=f"split vs fp32 {shape}")
+    assert s.mean() > 0.005
+
+
+def test_split_sparse_equals_split_dense_geometry(dev):
+    """Split weights with a tile mask walk hi and lo chunks of the active
+    activation chunks only; equal to the all-chunks launch bit for bit."""
+    ops = _ops()
+    T, B, C, H, W = 4, 4, 256, 14, 14
+    x = workloads.block_sparse_spikes(T, B, C, H, W, 0.9, seed=41)
+    _, w, scale, shift = _case(1, 1, C, C, 1, 1, 3, seed=42)
+    xp = ops.pack_tbchw(x.to(dev))
+    wp2, pre = ops.pack_conv_weight_split(w.to(dev), xp.shape[-1])
+    sc = (scale / pre).to(dev)
+    mask = ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1)
+    a = ops.conv_bn_lif(xp, wp2, sc, shift.to(dev), 1, 1, tile_mask=mask, precision="split")
+    b = ops.conv_bn_lif(xp, wp2, sc, shift.to(dev), 1, 1, tile_mask=torch.full_like(mask, -1),
+                        precision="split")
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_split_weight_pack(dev):
+    """hi + lo reproduces w * prescale to 22 bits; hi is fp16(w * prescale)."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(32, 20, 3, 3, generator=g) * 0.05
+    wp2, pre = ops.pack_conv_weight_split(w.to(dev), 32)
+    wp2 = wp2.cpu().float().reshape(32, 3, 3, 2, 32)
+    ref = (w * pre).permute(0, 2, 3, 1)
+    assert torch.equal(wp2[..., 0, :20], ref.half().float())
+    rec = wp2[..., 0, :20] + wp2[..., 1, :20]
+    assert (rec - ref).abs().max() <= ref.abs().max() * 2.0 ** -21
+    assert wp2[..., 20:].abs().max() == 0
+    assert 2.0 ** 13 <= float((w * pre).abs().max()) < 2.0 ** 14
 
 
 def test_conv_golden_reference(dev, golden_dir):
@@ -214,3 +303,41 @@ def test_im2col_pack(dev, shape):
     ref = torch.zeros(B, Ho, Wo, T, Kp)
     ref[..., :k * k * C] = cols
     assert torch.equal(y, ref.half())
+
+
+@pytest.mark.parametrize("shape", [(4, 2, 3, 32, 32, 3, 1, 1), (2, 3, 3, 17, 13, 7, 2, 3)])
+def test_im2col_split_stem(dev, shape):
+    """Split stem: the im2col pack carries the real-valued input as hi + lo and
+    the weight row [w, w] as hi + lo; the conv then meets the fp32 oracle at
+    the fp32 tolerance."""
+    ops = _ops()
+    T, B, C, H, W, k, s_, p = shape
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(T, B, C, H, W, generator=g)
+    y = ops.pack_im2col_split(x.to(dev), k, s_, p).cpu().float()
+    KK = k * k * C
+    hi = ops.pack_im2col(x.to(dev), k, s_, p, y.shape[-1]).cpu().float()
+    assert torch.equal(y[..., :KK], hi[..., :KK])
+    # hi + lo reproduces the fp32 input to 22 bits
+    Ho_ = (H + 2 * p - k) // s_ + 1
+    Wo_ = (W + 2 * p - k) // s_ + 1
+    cols = torch.nn.functional.unfold(x.reshape(T * B, C, H, W), k, padding=p, stride=s_)
+    cols = cols.reshape(T, B, C, k * k, Ho_, Wo_).permute(1, 4, 5, 0, 3, 2).reshape(B, Ho_, Wo_, T, KK)
+    err = (y[..., :KK] + y[..., KK:2 * KK] - cols).abs()
+    assert (err <= cols.abs() * 2.0 ** -21 + 2.0 ** -24).all()
+    Cout = 64
+    w = torch.randn(Cout, C, k, k, generator=g) * (2.0 / KK) ** 0.5
+    scale = torch.rand(Cout, generator=g) * 0.4 + 0.8
+    shift = torch.randn(Cout, generator=g) * 0.3
+    wp2, pre = ops.im2col_weight_split(w.to(dev), y.shape[-1])
+    yd = ops.pack_im2col_split(x.to(dev), k, s_, p, y.shape[-1])
+    Bq, Ho, Wo = yd.shape[0], yd.shape[1], yd.shape[2]
+    v = torch.empty(Bq, Ho, Wo, Cout, device=dev)
+    out = ops.conv_bn_lif(yd, wp2, (scale / pre).to(dev), shift.to(dev), 1, 0, v_out=v,
+                          precision="split")
+    sg = ops.unpack_bhwtc(out).cpu().numpy()
+    vg = ops.v_to_nchw(v).cpu().numpy()
+    s32, v32, z32 = oracle.conv_bn_lif(x, w, scale, shift, s_, p, return_z=True)
+    _, _, h32 = lif_trace(z32)
+    check_lif_parity(sg, vg, s32, v32, h32, v_tol=1e-4, near_tol=1e-4, max_flip_rate=1e-4,
+                     what=f"split stem {shape}")

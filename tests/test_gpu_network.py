@@ -210,3 +210,127 @@ def test_linear_lif_and_bn_add_lif(dev):
     z = oracle.conv.conv_z(xs, conv.weight.detach(), scale, shift, 1, 1, operand_dtype=torch.float16).numpy()
     s_o, v_o, h = lif_trace((z + ident.numpy()).astype(np.float32))
     check_lif_parity(out, None, s_o, None, h, what="conv_bn_add_lif")
+
+
+def _plan_layer_spikes(plan):
+    """{oracle record name: spikes [T,B,C,H,W]} of every LIF layer of a SEW plan
+    (the SEW ADD output minus its identity gives the LIF spikes)."""
+    from catfuse_b200 import ops
+    from catfuse_b200.network import ConvStep
+    out = {}
+    for st in plan.steps:
+        if not isinstance(st, ConvStep) or st.lif is None:
+            continue
+        y = ops.unpack_bhwtc(plan.acts[st.dst]).cpu()
+        if st.identity is not None and st.res_mode in ("ADD", "add"):
+            y = y - ops.unpack_bhwtc(plan.acts[st.identity]).cpu()
+        name = st.name
+        if name == "stem":
+            key = "sn1"
+        elif name.endswith(".conv1"):
+            key = name[:-len(".conv1")] + ".sn1"
+        elif name.endswith(".conv2"):
+            key = name[:-len(".conv2")] + ".sn2"
+        else:
+            key = name[:-len(".downsample")] + ".downsample_sn"
+        out[key] = y.numpy()
+    return out
+
+
+def test_sew_resnet18_split_precision_end_to_end_vs_fp32(dev):
+    """Config 1 (B=64, T=4) end to end, no teacher forcing, against the fp32
+    oracle: with split (hi + lo) weights and stem input every LIF layer's
+    spike-flip rate is <= 1e-4 and the T-summed classifier argmax agrees on
+    every sample -- the reference's end-to-end gate
+    (experiments/exp_40_end_to_end_v2.py:102-166)."""
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import functional
+    net, x = _sew_net(B=64, seed=0)
+    params = {k: v.detach().float() for k, v in net.state_dict().items()}
+    model, stats = optimize(net, device=dev, T=4, precision="split")
+    assert stats["native_plan"]
+    functional.reset_net(model)
+    logits = model(x.to(dev)).cpu()
+    plan = model.plan_for(x.to(dev))
+    record = []
+    ref = oracle.sew_resnet18_forward(x, params, record=record)
+    got = _plan_layer_spikes(plan)
+    assert len(got) == len(record) == 20
+    worst = 0.0
+    for name, s_ref, _ in record:
+        rate = float((got[name] != s_ref.numpy()).mean())
+        worst = max(worst, rate)
+        assert rate <= 1e-4, f"{name}: flip rate {rate:.2e}"
+    agree = (logits.sum(0).argmax(-1) == ref.sum(0).argmax(-1)).float().mean()
+    assert agree == 1.0, f"classifier agreement {agree}"
+    rel = (logits - ref).abs().max() / ref.abs().max()
+    print(f"split precision B=64: worst per-layer flip rate {worst:.2e}, logits rel err {rel:.2e}")
+
+
+def test_sew_resnet18_fp16_teacher_forced_b64(dev):
+    """fp16-operand mode at config 1's batch: every layer, fed its own input,
+    meets the per-layer gates against the fp16-operand oracle."""
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import functional
+    net, x = _sew_net(B=64, seed=2)
+    model, _ = optimize(net, device=dev, T=4)
+    functional.reset_net(model)
+    model(x.to(dev))
+    plan = model.plan_for(x.to(dev))
+    assert _teacher_forced_layers(plan, dev) <= 1e-4
+
+
+def test_forward_with_k_invariance(dev):
+    """SparseFlow.forward_with_k: TimeBlock(K) with v carried through the
+    StateBuffer gives the K=T output bit for bit for K in {1, 2, 4, T}
+    (the reference's tests/parity_suite_smoke.py:61-117)."""
+    from catfuse_b200 import patterns
+    from catfuse_b200.sj import layer, neuron
+    g = torch.Generator().manual_seed(13)
+    conv = layer.Conv2d(64, 128, 3, 1, 1, bias=False)
+    bn = layer.BatchNorm2d(128)
+    with torch.no_grad():
+        conv.weight.copy_(torch.randn(conv.weight.shape, generator=g) * 0.08)
+        bn.running_mean.copy_(torch.randn(128, generator=g) * 0.1)
+        bn.running_var.copy_(torch.rand(128, generator=g) + 0.5)
+    bn.eval()
+    lif = neuron.LIFNode(tau=2.0, step_mode="m")
+    T = 8
+    x = (torch.rand(T, 2, 64, 12, 12, generator=g) < 0.2).float().to(dev)
+    m = patterns.STFusionConvBNLIF.from_sj_modules(conv, bn, lif).to(dev)
+    impl = m._impl_sparse
+    outs = {}
+    for K in (1, 2, 4, T):
+        m.reset()
+        outs[K] = impl.forward_with_k(x, m.spec, m._ensure_params(), m.state, K=K)
+        v = m.state.tensor.clone()
+        if K == T:
+            vT = v
+    for K in (1, 2, 4):
+        assert torch.equal(outs[K], outs[T]), f"K={K}"
+    assert outs[T].sum() > 0
+    # and the dense implementation agrees with the oracle at fp16 operands
+    scale, shift = oracle.fold_bn(bn.weight.detach(), bn.bias.detach(), bn.running_mean,
+                                  bn.running_var)
+    s_o, v_o, z = oracle.conv_bn_lif(x.cpu(), conv.weight.detach(), scale, shift, 1, 1,
+                                     operand_dtype=torch.float16, return_z=True)
+    _, _, h = lif_trace(z)
+    check_lif_parity(outs[T].cpu().numpy(), vT.cpu().numpy(), s_o, v_o, h, what="forward_with_k")
+
+
+def test_avgpool_fc_head(dev):
+    """avgpool -> flatten -> fc over x[B,H,W,T,C] fp16 (the ResNet head)."""
+    from catfuse_b200 import ops
+    g = torch.Generator().manual_seed(17)
+    T, B, C, H, W, K = 4, 5, 512, 4, 4, 10
+    x = ((torch.rand(T, B, C, H, W, generator=g) < 0.3).float()
+         + (torch.rand(T, B, C, H, W, generator=g) < 0.2).float())   # SEW counts {0,1,2}
+    fc_w = torch.randn(K, C, generator=g) * 0.05
+    fc_b = torch.randn(K, generator=g) * 0.1
+    xp = ops.pack_tbchw(x.to(dev))
+    out = ops.avgpool_fc(xp, fc_w.to(dev), fc_b.to(dev)).cpu()
+    ref = torch.nn.functional.linear(x.double().mean(dim=(3, 4)), fc_w.double(), fc_b.double())
+    assert (out.double() - ref).abs().max() <= 1e-5
+    out0 = ops.avgpool_fc(xp, fc_w.to(dev), None).cpu()
+    ref0 = torch.nn.functional.linear(x.double().mean(dim=(3, 4)), fc_w.double())
+    assert (out0.double() - ref0).abs().max() <= 1e-5
