@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -80,11 +81,12 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+        fd, name = tempfile.mkstemp(prefix="catfuse_clocks_", suffix=".csv")
+        os.close(fd)
+        self.path = Path(name)
 
     def start(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -110,9 +112,14 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
+        text = self.path.read_text()
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
+        for line in text.splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -130,18 +137,51 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_model(device, batch, seed=0):
+def build_model(device, batch, seed=0, precision="fp16"):
     from catfuse_b200 import optimize
     from catfuse_b200.sj import zoo
     net = zoo.init_random_(zoo.build_sew_resnet18_cifar(), seed)
     g = torch.Generator().manual_seed(1000 + seed)
-    calib = torch.randn(batch, 3, 32, 32, generator=g).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+    calib = torch.randn(BATCH, 3, 32, 32, generator=g).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
     zoo.calibrate_bn_(net, calib)
-    model, stats = optimize(net.eval(), device=device, T=T_STEPS)
+    model, stats = optimize(net.eval(), device=device, T=T_STEPS, precision=precision)
     return model, stats, net
 
 
-def cpu_baseline(batch=16, budget_s=12.0):
+def time_plan(plan, steps, flush, dist=None, gathered=None):
+    """Per-step CUDA-event times (ms) of the graphed forward, L2 flushed
+    between steps outside the events; returns the list of step times."""
+    def step():
+        plan.fresh = True            # reset_net: every step starts from v = 0
+        logits = plan.run(use_graph=True)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, logits)
+        return logits
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for s, e in evs:
+        flush.fill_(1.0)
+        s.record()
+        step()
+        e.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def max_over_ranks(x, dev, dist):
+    t = torch.tensor([float(x)], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(batch=BATCH, budget_s=12.0):
     """The reference's CPU path (SJ semantics in PyTorch; oracle restatement)
     on the host cores, a bounded sample of the workload."""
     import oracle
@@ -172,25 +212,98 @@ def run_reference(args):
     if rank != 0:
         return 0
     # At most 8 bounded CPU samples (~1 minute in total) whatever --steps asks:
-    # each step is a multi-second sample of the CPU workload, not one forward.
+    # each step is a multi-second sample of the CPU workload (B=64 forwards,
+    # the GPU arm's configuration), not one forward.
     n_ref = max(1, min(args.steps, 8))
     budget = max(2.0, min(20.0, 60.0 / (n_ref + min(args.warmup, 3))))
     for _ in range(min(args.warmup, 3)):
         cpu_baseline(batch=8, budget_s=0.5)
-    vals = [cpu_baseline(batch=16, budget_s=budget) for _ in range(n_ref)]
+    vals = [cpu_baseline(batch=BATCH, budget_s=budget) for _ in range(n_ref)]
     v = statistics.median(x["value"] for x in vals)
     base = vals[0]
     base["value"] = v
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * 16 / v, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * BATCH / v, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference", "cpu_samples": n_ref,
             "config": {"workload": "SEW-ResNet18 CIFAR T=4 forward (reference CPU path)",
-                       "global_batch": 16, "seq_len": T_STEPS, "parallelism": "cpu"},
+                       "global_batch": BATCH, "seq_len": T_STEPS, "parallelism": "cpu"},
             "cpu_baseline": base,
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def conv_roofline(plan, flush, peaks, peak_src):
+    """The forward's conv launches replayed alone as one CUDA graph (same
+    inputs, same order, L2 flushed before each replay), plus each launch timed
+    alone (eager, L2 flushed before it) for the per-layer fractions."""
+    from catfuse_b200.network import ConvStep
+    from catfuse_b200 import ops
+
+    def launch(st):
+        ident = plan.acts[st.identity] if st.identity is not None else None
+        mode = "z_only" if st.lif is None else (st.res_mode if ident is not None else "none")
+        ops.conv_bn_lif(plan.acts[st.src], st.wp, st.scale, st.shift, st.stride, st.pad,
+                        identity=ident if st.lif is not None else None, res_mode=mode,
+                        v_in=None, v_out=st.v, lif=st.lif or ops.LIFConfig(),
+                        out=plan.acts[st.dst], precision=st.prec)
+
+    convs = [st for st in plan.steps if isinstance(st, ConvStep)]
+
+    def conv_launches():
+        for st in convs:
+            launch(st)
+
+    plan.fresh = True
+    plan.pack_input()
+    conv_launches()                      # warm-up (also fills every activation)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    conv_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(conv_graph, stream=side):
+        conv_launches()
+    torch.cuda.synchronize()
+    conv_ms = []
+    for _ in range(5):
+        flush.fill_(1.0)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        conv_graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        conv_ms.append(a.elapsed_time(b))
+    conv_ms_fwd = sum(conv_ms) / len(conv_ms)
+    peak = peaks["bf16_tflops"]
+    per_layer = []
+    for st in convs:
+        b_, ho, wo, t_, co = plan.shapes[st.dst]
+        spec = st.native.spec
+        fl = 2.0 * t_ * b_ * ho * wo * co * spec.in_channels * spec.kernel_size ** 2
+        ts = []
+        for _ in range(5):
+            flush.fill_(1.0)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            launch(st)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        us = 1000.0 * statistics.median(ts)
+        per_layer.append({"layer": st.name, "us": round(us, 2),
+                          "tflops": round(fl / us / 1e6, 1),
+                          "frac": round(fl / us / 1e6 / peak, 3)})
+    flops = _conv_flops(plan)
+    achieved = flops / (conv_ms_fwd / 1000.0) / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": peak,
+            "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": _traffic_from_profiles(), "peak_source": f"{peak_src} bf16_tflops (burst)",
+            "kernel": "conv_t_kernel / conv_bn_lif_kernel (the 20 conv launches of one "
+                      "forward, replayed as one CUDA graph, L2 flushed before each replay)",
+            "flops_per_forward": flops, "conv_ms_per_forward": conv_ms_fwd,
+            "launches_per_forward": len(convs), "per_layer": per_layer}
 
 
 def main():
@@ -201,6 +314,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the fp32-mode and strong-scaling side measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -227,93 +342,25 @@ def main():
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     gathered = torch.empty((world, T_STEPS, B, 10), device=dev) if world > 1 else None
 
-    def step():
-        plan.fresh = True            # reset_net: every step starts from v = 0
-        logits = plan.run(use_graph=True)
-        if dist is not None:
-            dist.all_gather_into_tensor(gathered, logits)
-        return logits
-
     for _ in range(args.warmup):
-        step()
+        plan.fresh = True
+        plan.run(use_graph=True)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, plan.logits)
     torch.cuda.synchronize()
 
     # ---- value: device-resident inputs, per-step CUDA events, L2 flushed ----
     sampler = ClockSampler(local)
     sampler.start()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    for s, e in evs:
-        flush.fill_(1.0)
-        s.record()
-        step()
-        e.record()
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
+    step_ms = time_plan(plan, args.steps, flush, dist, gathered)
     clocks = sampler.stop()
-    step_ms = [s.elapsed_time(e) for s, e in evs]
-    total_ms = sum(step_ms)
-    t = torch.tensor([total_ms], device=dev)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
+    total_ms = max_over_ranks(sum(step_ms), dev, dist)
     ms_per_step = total_ms / args.steps
     value = world * B * args.steps / (total_ms / 1000.0)
 
-    # ---- kernel roofline: the forward's 20 conv launches replayed alone ------
-    # as one CUDA graph (same inputs, same order, L2 flushed before each
-    # replay), timed with events on the replaying stream.
-    from catfuse_b200.network import ConvStep
-    from catfuse_b200 import ops
-
-    def conv_launches():
-        for st in plan.steps:
-            if not isinstance(st, ConvStep):
-                continue
-            ident = plan.acts[st.identity] if st.identity is not None else None
-            mode = "z_only" if st.lif is None else (st.res_mode if ident is not None else "none")
-            ops.conv_bn_lif(plan.acts[st.src], st.wp, st.scale, st.shift, st.stride, st.pad,
-                            identity=ident if st.lif is not None else None, res_mode=mode,
-                            v_in=None, v_out=st.v, lif=st.lif or ops.LIFConfig(),
-                            out=plan.acts[st.dst])
-
-    plan.fresh = True
-    plan.pack_input()
-    conv_launches()                      # warm-up (also fills every activation)
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    conv_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(conv_graph, stream=side):
-        conv_launches()
-    torch.cuda.synchronize()
-    conv_ms = []
-    for _ in range(5):
-        flush.fill_(1.0)
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        conv_graph.replay()
-        b.record()
-        torch.cuda.synchronize()
-        conv_ms.append(a.elapsed_time(b))
-    n_conv = sum(1 for st in plan.steps if isinstance(st, ConvStep))
-    conv_ms_fwd = sum(conv_ms) / len(conv_ms)
-    flops = _conv_flops(plan)
     peaks, peak_src = _peaks()
-    achieved = flops / (conv_ms_fwd / 1000.0) / 1e12
-    traffic = _traffic_from_profiles()
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                "traffic": traffic, "peak_source": f"{peak_src} bf16_tflops (burst)",
-                "kernel": "conv_t_kernel / conv_bn_lif_kernel (the 20 conv launches of one "
-                          "forward, replayed as one CUDA graph, L2 flushed before each replay)",
-                "flops_per_forward": flops, "conv_ms_per_forward": conv_ms_fwd,
-                "launches_per_forward": n_conv,
-                "share_of_step": conv_ms_fwd / ms_per_step}
+    roofline = conv_roofline(plan, flush, peaks, peak_src)
+    roofline["share_of_step"] = roofline["conv_ms_per_forward"] / ms_per_step
 
     # ---- e2e through the public API (host buffers, copies inside) -----------
     pinned = images.pin_memory()
@@ -341,11 +388,42 @@ def main():
         e2e_step()
     b.record()
     torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b)
-    t = torch.tensor([e2e_ms], device=dev)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * B * args.steps / (float(t.item()) / 1000.0)
+    e2e_ms = max_over_ranks(a.elapsed_time(b), dev, dist)
+    e2e_value = world * B * args.steps / (e2e_ms / 1000.0)
+
+    extras = {}
+    if not args.no_extras:
+        n_side = max(20, min(args.steps, 100))
+        # fp32-faithful mode (exact integer weight planes), same protocol
+        m32, _, _ = build_model(dev, args.batch, precision="fp32")
+        p32 = m32.plan_for(x_dev)
+        p32.x_in.copy_(x_dev)
+        for _ in range(3):
+            p32.fresh = True
+            p32.run(use_graph=True)
+        t32 = max_over_ranks(sum(time_plan(p32, n_side, flush, dist, gathered)), dev, dist)
+        extras["precision_modes"] = {
+            "fp16": {"value": value, "note": "fp16 weights (the reference GPU path's TF32/fp16 "
+                                             "operand precision)"},
+            "fp32": {"value": world * B * n_side / (t32 / 1000.0), "steps": n_side,
+                     "note": "fp32-faithful: exact integer weight planes, hi+lo stem"}}
+        del m32, p32
+        if world > 1 and BATCH % world == 0:
+            # strong scaling: the global batch of 64 sharded over the ranks
+            bs = BATCH // world
+            ms, _, _ = build_model(dev, bs)
+            xs = x_dev[:, :bs].contiguous()
+            ps = ms.plan_for(xs)
+            ps.x_in.copy_(xs)
+            gs = torch.empty((world, T_STEPS, bs, 10), device=dev)
+            for _ in range(3):
+                ps.fresh = True
+                ps.run(use_graph=True)
+                dist.all_gather_into_tensor(gs, ps.logits)
+            ts = max_over_ranks(sum(time_plan(ps, n_side, flush, dist, gs)), dev, dist)
+            extras["strong_scaling"] = {"global_batch": BATCH, "per_gpu_batch": bs,
+                                        "value": BATCH * n_side / (ts / 1000.0),
+                                        "ms_per_step": ts / n_side, "steps": n_side}
 
     if rank == 0:
         line = {
@@ -357,7 +435,8 @@ def main():
                        "per_gpu_batch": B, "seq_len": T_STEPS, "parallelism": f"dp{world}",
                        "l2": "flushed (256 MB write) between timed steps",
                        "weights": "random init (seed 0), BN statistics calibrated on synthetic data",
-                       "operands": "fp16 spikes/weights, fp32 accumulate + LIF"},
+                       "operands": "fp16 spikes/weights, fp32 accumulate + LIF",
+                       "precision": "fp16"},
             "gpu_launches": plan.launches() * args.steps,
             "roofline": roofline,
             "e2e": {"value": e2e_value, "unit": UNIT,
@@ -366,6 +445,7 @@ def main():
             "clocks": clocks,
             "routing": {k: v for k, v in stats["patterns_matched"].items()},
         }
+        line.update(extras)
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

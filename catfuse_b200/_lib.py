@@ -67,6 +67,10 @@ SIGNATURES = {
     "cf_pack_conv_weight_split": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "cf_pack_im2col_split": (_INT, [_P, _INT, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                     _I64, _P]),
+    "cf_conv_bn_lif_planes": (_INT, [_P, _P, _P, _P, _P, _INT, _P, _P, _P, _I64, _I64, _I64,
+                                     _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _INT,
+                                     _INT, _P]),
+    "cf_pack_conv_weight_planes": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "cf_set_wait_limit": (_INT, [ctypes.c_uint32]),
     "cf_test_arm_stalled_load": (_INT, [_INT]),
     "cf_avgpool_fc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),

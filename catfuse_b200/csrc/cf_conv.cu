@@ -140,8 +140,10 @@ int choose_bk(int Cin_p, bool sparse) {
   return 16;
 }
 
+// nplanes = 3: integer weight planes in three accumulators, which fit TMEM
+// (512 columns) only as single-buffered N = 128 tiles of the channel-major kernel.
 int make_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout, int64_t Cin_p,
-                  int64_t stride, bool sparse, Geometry& g) {
+                  int64_t stride, bool sparse, Geometry& g, int nplanes = 1) {
   const int tc = (int)(T < kMaxTP ? T : kMaxTP);
   g.TP = next_pow2(tc);
   g.BK = choose_bk((int)Cin_p, sparse);
@@ -152,12 +154,16 @@ int make_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout, in
     g.BN = Cout % 128 == 0 ? 128 : 64;
     g.NR = 256;
     choose_box(g.NR / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
-    if ((long)g.n_mtiles * (Cout / g.BN) < (148 * 3) / 4) {
+    if (nplanes > 1 || (long)g.n_mtiles * (Cout / g.BN) < (148 * 3) / 4) {
       g.NR = 128;
       choose_box(g.NR / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
     }
     return CF_OK;
   }
+  if (nplanes > 1)
+    return fail(CF_ERR_UNSUPPORTED,
+                "integer weight planes need the channel-major kernel (Cout %% 128 == 0, or "
+                "Cout %% 64 == 0 with Cin_p >= 64)");
   g.tmode = 0;
   g.NR = 128;
   choose_box(128 / g.TP, (int)B, (int)Ho, (int)Wo, (int)stride, g);
@@ -196,7 +202,7 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
                      void* out, const uint32_t* tile_mask, int64_t T, int64_t B, int64_t H,
                      int64_t W, int64_t Cin_p, int64_t Cout, int64_t KH, int64_t KW,
                      int64_t stride, int64_t pad, float tau, float v_th, float v_reset,
-                     int hard_reset, int decay_input, int wsplit, cudaStream_t stream) {
+                     int hard_reset, int decay_input, int wparts, cudaStream_t stream) {
   if (!x || !wp || !out) return fail(CF_ERR_INVALID_ARG, "x, wp and out must not be NULL");
   if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin_p <= 0 || Cout <= 0 || KH <= 0 || KW <= 0 ||
       stride <= 0 || pad < 0)
@@ -222,12 +228,16 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   if (int rc = require_sm100()) return rc;
 
   Geometry g{};
-  if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, tile_mask != nullptr, g)) return rc;
+  const int nplanes = wparts == 3 ? 3 : 1;
+  if (nplanes > 1 && tile_mask)
+    return fail(CF_ERR_UNSUPPORTED, "integer weight planes run dense only (no tile mask)");
+  if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, tile_mask != nullptr, g, nplanes))
+    return rc;
   const int n_kx = g.n_kc;  // activation chunks per tap
-  if (wsplit) g.n_kc *= 2;   // split weights: hi chunks, then lo chunks
+  g.n_kc *= wparts;          // weight chunks: part 0 chunks, then part 1, ...
   if (tile_mask && g.n_kc > 32)
     return fail(CF_ERR_UNSUPPORTED, "sparse mode supports at most 32 channel chunks");
-  const int64_t Cin_w = wsplit ? 2 * Cin_p : Cin_p;
+  const int64_t Cin_w = wparts * Cin_p;
 
   auto encode = get_encode_fn();
   if (!encode) return fail(CF_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
@@ -294,6 +304,8 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.Cout = (int)Cout; args.Cin_p = (int)Cin_p;
   args.Cin_w = (int)Cin_w;
   args.n_kx = n_kx;
+  args.wparts = wparts;
+  args.nplanes = nplanes;
   args.KH = (int)KH; args.KW = (int)KW; args.stride = (int)stride; args.pad = (int)pad;
   args.Wb = g.Wb; args.Hb = g.Hb; args.Bb = g.Bb;
   args.n_wt = g.n_wt; args.n_ht = g.n_ht; args.n_mtiles = g.n_mtiles;
@@ -310,8 +322,11 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   if (g.tmode) {
     args.MT = g.BN;
     args.idesc = make_idesc_f16(g.BN, g.NR);
-    args.tmem_cols = (uint32_t)(2 * g.NR);
+    args.nbuf = nplanes > 1 ? 1 : 2;  // 3 planes x 128 columns leave no room for a second buffer
+    const uint32_t cols = (uint32_t)(args.nbuf * nplanes * g.NR);
+    args.tmem_cols = cols <= 256 ? (cols <= 128 ? 128u : 256u) : 512u;  // a power of two
   } else {
+    args.nbuf = 2;
     args.idesc = make_idesc_f16(128, g.BN);
     args.tmem_cols = (uint32_t)(2 * g.BN < 32 ? 32 : 2 * g.BN);
   }
@@ -401,12 +416,14 @@ int cf_conv_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout,
 }
 
 int cf_conv_geometry_ex(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout,
-                        int64_t Cin_p, int64_t stride, int sparse, int32_t* out6) {
+                        int64_t Cin_p, int64_t stride, int flags, int32_t* out6) {
+  const bool sparse = (flags & 1) != 0;
+  const int nplanes = (flags & 2) ? 3 : 1;
   if (!out6 || T <= 0 || B <= 0 || Ho <= 0 || Wo <= 0 || Cout <= 0 || Cin_p <= 0 ||
       Cin_p % 16 || stride <= 0)
     return fail(CF_ERR_INVALID_ARG, "bad geometry query");
   Geometry g{};
-  if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, sparse != 0, g)) return rc;
+  if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, sparse, g, nplanes)) return rc;
   out6[0] = g.TP; out6[1] = g.Wb; out6[2] = g.Hb; out6[3] = g.Bb;
   out6[4] = g.n_mtiles; out6[5] = g.BN;
   return CF_OK;
@@ -425,7 +442,7 @@ int cf_conv_bn_lif(const void* x, const void* wp, const float* scale, const floa
                    int decay_input, void* stream) {
   return conv_bn_lif_impl(x, wp, scale, shift, identity, res_mode, v_in, v_out, out, tile_mask, T,
                           B, H, W, Cin_p, Cout, KH, KW, stride, pad, tau, v_threshold, v_reset,
-                          hard_reset, decay_input, 0, static_cast<cudaStream_t>(stream));
+                          hard_reset, decay_input, 1, static_cast<cudaStream_t>(stream));
 }
 
 int cf_conv_bn_lif_split(const void* x, const void* wp2, const float* scale, const float* shift,
@@ -436,7 +453,18 @@ int cf_conv_bn_lif_split(const void* x, const void* wp2, const float* scale, con
                          int hard_reset, int decay_input, void* stream) {
   return conv_bn_lif_impl(x, wp2, scale, shift, identity, res_mode, v_in, v_out, out, tile_mask, T,
                           B, H, W, Cin_p, Cout, KH, KW, stride, pad, tau, v_threshold, v_reset,
-                          hard_reset, decay_input, 1, static_cast<cudaStream_t>(stream));
+                          hard_reset, decay_input, 2, static_cast<cudaStream_t>(stream));
+}
+
+int cf_conv_bn_lif_planes(const void* x, const void* wq, const float* scale, const float* shift,
+                          const void* identity, int res_mode, const float* v_in, float* v_out,
+                          void* out, int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin_p,
+                          int64_t Cout, int64_t KH, int64_t KW, int64_t stride, int64_t pad,
+                          float tau, float v_threshold, float v_reset, int hard_reset,
+                          int decay_input, void* stream) {
+  return conv_bn_lif_impl(x, wq, scale, shift, identity, res_mode, v_in, v_out, out, nullptr, T,
+                          B, H, W, Cin_p, Cout, KH, KW, stride, pad, tau, v_threshold, v_reset,
+                          hard_reset, decay_input, 3, static_cast<cudaStream_t>(stream));
 }
 
 int cf_linear_bn_lif(const void* x, const void* w, const float* scale, const float* shift,
@@ -447,7 +475,7 @@ int cf_linear_bn_lif(const void* x, const void* w, const float* scale, const flo
   // Tokens are pixels of an L x 1 map: a 1x1 convolution.
   return conv_bn_lif_impl(x, w, scale, shift, identity, res_mode, v_in, v_out, out, nullptr, T, B,
                           L, 1, Cin_p, Cout, 1, 1, 1, 0, tau, v_threshold, v_reset, hard_reset,
-                          decay_input, 0, static_cast<cudaStream_t>(stream));
+                          decay_input, 1, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

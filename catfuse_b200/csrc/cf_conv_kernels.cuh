@@ -75,8 +75,11 @@ struct ConvArgs {
   int t0;       // first step of this launch
   int tcount;   // steps in this launch (<= TP)
   int B, Ho, Wo, Cout, Cin_p;
-  int Cin_w;        // weight channels per tap: Cin_p, or 2*Cin_p for split (hi, lo) weights
-  int n_kx;         // activation channel chunks per tap (n_kc / 2 for split weights)
+  int Cin_w;        // weight channels per tap: wparts * Cin_p
+  int wparts;       // weight parts per tap: 1 (fp16), 2 (hi, lo) or 3 (integer digit planes)
+  int n_kx;         // activation channel chunks per tap (n_kc / wparts)
+  int nplanes;      // channel-major: separate accumulators (1, or 3 for integer weight planes)
+  int nbuf;         // channel-major: accumulator buffers in TMEM (2 = double-buffered, or 1)
   int KH, KW, stride, pad;
   int Wb, Hb, Bb;
   int n_wt, n_ht, n_mtiles, n_ntiles, n_tiles;
@@ -143,20 +146,26 @@ __device__ __forceinline__ bool warp_wait_or_abort(uint64_t* bar, uint32_t parit
   return false;
 }
 
-// Chunk mask of a tile: bit kc = weight chunk kc has work.  Split weights walk
-// 2 * n_kx chunks (hi then lo) over the same activation chunks, so an
-// activation chunk mask is repeated for the lo half.
+// Chunk mask of a tile: bit kc = weight chunk kc has work.  Multi-part
+// weights walk wparts * n_kx chunks (part 0, then part 1, ...) over the same
+// activation chunks, so an activation chunk mask is repeated for every part.
+// Sparse launches have at most 32 chunks; dense ones may have more (chunk_on).
 __device__ __forceinline__ uint32_t tile_kmask(const ConvArgs& a, int mt) {
   if (!a.tile_mask) return a.kc_all;
-  uint32_t m = __ldg(a.tile_mask + mt);
-  if (a.n_kx != a.n_kc) m |= m << a.n_kx;
-  return m & a.kc_all;
+  const uint32_t m = __ldg(a.tile_mask + mt);
+  uint32_t r = m;
+  for (int p = 1; p < a.wparts; ++p) r |= m << (p * a.n_kx);
+  return r & a.kc_all;
 }
 
-// Activation channel chunk read by weight chunk kc (the lo half of split
-// weights multiplies the same activations as the hi half).
+__device__ __forceinline__ bool chunk_on(uint32_t km, int kc) {
+  return kc >= 32 || ((km >> kc) & 1u);
+}
+
+// Activation channel chunk read by weight chunk kc (every weight part
+// multiplies the same activations).
 __device__ __forceinline__ int xchunk(const ConvArgs& a, int kc) {
-  return kc < a.n_kx ? kc : kc - a.n_kx;
+  return kc >= 2 * a.n_kx ? kc - 2 * a.n_kx : (kc >= a.n_kx ? kc - a.n_kx : kc);
 }
 
 // LIF step for the common configuration (decay_input, hard reset to 0, tau a
@@ -395,7 +404,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         for (int kh = 0; kh < KHs && ok; ++kh) {
           for (int kw = 0; kw < KWs && ok; ++kw, ++tap) {
             for (int kc = 0; kc < a.n_kc; ++kc) {
-              if (!((km >> kc) & 1u)) continue;
+              if (!chunk_on(km, kc)) continue;
               const bool mine = owner == p;
               const int my_stage = stage;
               const uint32_t my_phase = phase;
@@ -492,7 +501,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               if (a.wres) {
                 if (kc) b_desc_w += b_step;
               }
-              if (!((km >> kc) & 1u)) continue;
+              if (!chunk_on(km, kc)) continue;
               if (!mbar_try_wait(&full_bar[stage], phase) &&
                   !wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag, a)) {
                 ok = false;
@@ -821,7 +830,39 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
   __syncwarp();  // the staging rows are reused by the next chunk
 }
 
-template <int TP, int RES, bool FAST>
+// Integer weight planes (PL = 3): the weight is quantised to a 30-bit integer
+// q = q2 * 2^20 + q1 * 2^10 + q0 with signed digits |q_i| <= 512, each digit
+// plane an fp16 operand holding exact integers.  With integer activations
+// (spike counts) every product and every partial sum is an integer below
+// 2^24, so each plane's fp32 TMEM accumulation is exact whatever the tensor
+// core's internal rounding; the planes sit in separate accumulators and the
+// epilogue joins them in fp64 (exact) before one rounding to fp32.
+template <int PL>
+__device__ __forceinline__ void load_acc(uint32_t taddr, uint32_t plane_cols, bool m128,
+                                         float (&r)[32]) {
+  if constexpr (PL == 1) {
+    if (m128) tmem_ld32(taddr, r);
+    else tmem_ld16x2_32(taddr, r);
+  } else {
+    // plane p (accumulator columns p * plane_cols on) holds sum x * q_{2-p}
+    float t[32];
+    double d[32];
+    if (m128) tmem_ld32(taddr, t);
+    else tmem_ld16x2_32(taddr, t);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) d[j] = (double)t[j] * 1048576.0;
+    if (m128) tmem_ld32(taddr + plane_cols, t);
+    else tmem_ld16x2_32(taddr + plane_cols, t);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) d[j] = fma((double)t[j], 1024.0, d[j]);
+    if (m128) tmem_ld32(taddr + 2 * plane_cols, t);
+    else tmem_ld16x2_32(taddr + 2 * plane_cols, t);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = (float)(d[j] + (double)t[j]);
+  }
+}
+
+template <int TP, int RES, bool FAST, int PL>
 __global__ void __launch_bounds__(kTThreads, 1)
     conv_t_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                   const ConvArgs a) {
@@ -916,7 +957,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         for (int gh = 0; gh < n_gh && ok; ++gh) {
           for (int gw = 0; gw < n_gw && ok; ++gw) {
             for (int kc = 0; kc < a.n_kc; ++kc) {
-              if (!((km >> kc) & 1u)) continue;
+              if (!chunk_on(km, kc)) continue;
               const bool mine = owner == p;
               const int my_stage = stage;
               const uint32_t my_phase = phase;
@@ -999,18 +1040,26 @@ __global__ void __launch_bounds__(kTThreads, 1)
         if (km == 0) {
           mbar_arrive(&tfull_bar[acc]);
         } else {
-          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * NR);
-          uint32_t accum = 0u;
+          const uint32_t d_base = tmem_base + (uint32_t)(acc * PL * NR);
+          uint32_t started = 0u;  // planes whose accumulator holds a first product
           const int n_g = n_gh * n_gw;
           for (int g = 0; g < n_g && ok; ++g) {
+            int plane = 0, pk = 0;  // weight plane of chunk kc (kc / n_kx), and kc % n_kx
             for (int kc = 0; kc < a.n_kc; ++kc) {
-              if (!((km >> kc) & 1u)) continue;
+              const int cur_plane = plane;
+              if (PL > 1 && ++pk == a.n_kx) {
+                pk = 0;
+                ++plane;
+              }
+              if (!chunk_on(km, kc)) continue;
               if (!mbar_try_wait(&full_bar[stage], phase) &&
                   !wait_or_abort(&full_bar[stage], phase, ERR_SITE_MMA_FULL, abort_flag, a)) {
                 ok = false;
                 break;
               }
               {
+                const uint32_t d_tmem = d_base + (uint32_t)(PL > 1 ? cur_plane * NR : 0);
+                uint32_t accum = (started >> cur_plane) & 1u;
                 uint64_t bd = xd, ad = wd;
                 for (int j = 0; j < nsub; ++j, bd += sub_step, ad += w_step) {
                   if (ksteps == 4) issue_kchunk<4>(d_tmem, ad, bd, a.idesc, accum);
@@ -1018,6 +1067,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                   else issue_kchunk<1>(d_tmem, ad, bd, a.idesc, accum);
                   accum = 1u;
                 }
+                started |= 1u << cur_plane;
               }
               umma_commit(&empty_bar[stage]);
               if (++stage == S) {
@@ -1034,8 +1084,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
           if (!ok) break;
           umma_commit(&tfull_bar[acc]);
         }
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
+        if (++acc == a.nbuf) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
       umma_commit(done_bar);
       for (uint32_t p = 0; p < kMaxPolls; ++p)
@@ -1077,14 +1129,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
       for (int ch = k; ch < n_chunk; ch += E) {
         const int col = ch * CW;
         float r[32];
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * NR + col);
+        const uint32_t taddr =
+            tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * PL * NR + col);
         if (!has_acc) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = 0.f;
-        } else if (MT == 128) {
-          tmem_ld32(taddr, r);
         } else {
-          tmem_ld16x2_32(taddr, r);
+          load_acc<PL>(taddr, (uint32_t)NR, MT == 128, r);
         }
         if (ch == last_chunk) {
           // Last read of this warp: hand the accumulator back to the MMA warp.
@@ -1108,8 +1159,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
                                                   stage, lane);
         }
       }
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (++acc == a.nbuf) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
     }
   }
 
@@ -1170,7 +1223,7 @@ int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, i
   return check_launch("conv_bn_lif launch");
 }
 
-template <int TP, int RES, bool FAST>
+template <int TP, int RES, bool FAST, int PL>
 int launch_t(const CUtensorMap& tmX, const CUtensorMap& tmW, ConvArgs args, int grid,
              cudaStream_t stream) {
   const int nsub = args.khbox ? args.KH : (args.kwgroup ? args.KW : 1);
@@ -1187,17 +1240,18 @@ int launch_t(const CUtensorMap& tmX, const CUtensorMap& tmW, ConvArgs args, int 
   int smem = fixed + stages * stage_bytes;
   if (smem < 120 * 1024) smem = 120 * 1024;  // one TMEM-owning CTA per SM
   static std::atomic<bool> attr_done[kMaxDevices];
-  if (int rc = allow_big_smem(reinterpret_cast<const void*>(conv_t_kernel<TP, RES, FAST>),
+  if (int rc = allow_big_smem(reinterpret_cast<const void*>(conv_t_kernel<TP, RES, FAST, PL>),
                               attr_done, "cudaFuncSetAttribute(conv_t)"))
     return rc;
-  conv_t_kernel<TP, RES, FAST><<<grid, kTThreads, smem, stream>>>(tmX, tmW, args);
+  conv_t_kernel<TP, RES, FAST, PL><<<grid, kTThreads, smem, stream>>>(tmX, tmW, args);
   return check_launch("conv_t launch");
 }
 
 template <int TP, int RES, bool FAST>
 int launch_any(const CUtensorMap& A, const CUtensorMap& W, const ConvArgs& args, int grid,
                cudaStream_t s) {
-  return args.tmode ? launch_t<TP, RES, FAST>(A, W, args, grid, s)
+  if (args.nplanes == 3) return launch_t<TP, RES, FAST, 3>(A, W, args, grid, s);
+  return args.tmode ? launch_t<TP, RES, FAST, 1>(A, W, args, grid, s)
                     : launch_inst<TP, RES, FAST>(A, W, args, grid, s);
 }
 

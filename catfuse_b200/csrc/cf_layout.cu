@@ -137,6 +137,36 @@ __global__ void pack_weight_split_kernel(const float* __restrict__ w, __half* __
   }
 }
 
+// Integer weight planes: q = rint(w * prescale) (|q| < 2^28 for the
+// prescale the caller picks), written as signed base-1024 digits
+// q = q2 * 2^20 + q1 * 2^10 + q0 with q1, q0 in [-512, 512) and |q2| <= 257,
+// each an exactly representable fp16 integer:
+// wq[co][kh][kw][p][ci] = q_{2-p}, i.e. the most significant plane first.
+__global__ void pack_weight_planes_kernel(const float* __restrict__ w, __half* __restrict__ wq,
+                                          int Cout, int Cin, int KH, int KW, int Cin_p,
+                                          float prescale) {
+  const int64_t n = (int64_t)Cout * KH * KW * Cin_p;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int ci = (int)(i % Cin_p);
+    const int64_t tap_row = i / Cin_p;  // (co, kh, kw)
+    int64_t r = tap_row;
+    const int kw = (int)(r % KW); r /= KW;
+    const int kh = (int)(r % KH);
+    const int co = (int)(r / KH);
+    long long q = 0;
+    if (ci < Cin) q = llrintf(__fmul_rn(w[(((int64_t)co * Cin + ci) * KH + kh) * KW + kw], prescale));
+    const long long q2 = (q + (1ll << 19)) >> 20;  // floor division: round to nearest digit
+    const long long rem = q - q2 * (1ll << 20);      // in [-2^19, 2^19)
+    const long long q1 = (rem + 512) >> 10;
+    const long long q0 = rem - q1 * 1024;            // in [-512, 512)
+    __half* dst = wq + tap_row * 3 * Cin_p + ci;
+    dst[0] = __float2half_rn((float)q2);
+    dst[Cin_p] = __float2half_rn((float)q1);
+    dst[2 * Cin_p] = __float2half_rn((float)q0);
+  }
+}
+
 // One CTA per (t, b): mean over H*W of x[b][:, :, t, :] into shared memory,
 // then one warp per class computes the fc dot product.
 __global__ void avgpool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
@@ -359,6 +389,23 @@ int cf_pack_im2col_split(const void* x, int x_fmt, void* y, int64_t T, int64_t B
                          int64_t H, int64_t W, int64_t k, int64_t stride, int64_t pad, int64_t Kp,
                          void* stream) {
   return im2col_impl(x, x_fmt, y, T, B, C, H, W, k, stride, pad, Kp, 1, stream);
+}
+
+int cf_pack_conv_weight_planes(const float* w, void* wq, int64_t Cout, int64_t Cin, int64_t KH,
+                               int64_t KW, int64_t Cin_p, float prescale, void* stream) {
+  if (!w || !wq) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (Cout <= 0 || Cin <= 0 || KH <= 0 || KW <= 0 || Cin_p < Cin || Cin_p % 16)
+    return fail(CF_ERR_INVALID_ARG, "bad weight shape (Cin_p >= Cin, Cin_p %% 16 == 0)");
+  int e = 0;
+  if (!(prescale > 0.f) || frexpf(prescale, &e) != 0.5f)
+    return fail(CF_ERR_INVALID_ARG, "prescale must be a positive power of two");
+  if (int rc = require_sm100()) return rc;
+  const int64_t n = Cout * KH * KW * Cin_p;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  pack_weight_planes_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      w, static_cast<__half*>(wq), (int)Cout, (int)Cin, (int)KH, (int)KW, (int)Cin_p, prescale);
+  return check_launch("pack_weight_planes launch");
 }
 
 int cf_pack_conv_weight_split(const float* w, void* wp2, int64_t Cout, int64_t Cin, int64_t KH,

@@ -33,8 +33,9 @@ class _WeightCache:
 
     def get(self, spec: ConvLIFSpec, params: ConvLIFParams, device, precision: str = "fp16"):
         """-> (packed weight, epilogue scale, epilogue shift) for ``precision``
-        ("fp16": wp[Cout,KH,KW,Cin_p]; "split": hi | lo weights with the
-        scale divided by their power-of-two prescale)."""
+        ("fp16": wp[Cout,KH,KW,Cin_p]; "split": hi | lo weights, "planes":
+        integer digit planes, each with the scale divided by the power-of-two
+        prescale of the packing)."""
         def tag(t):
             return None if t is None else (id(t), t.data_ptr(), t._version, t.device)
         key = (tag(params.weight), tag(params.bias), tag(params.bn_scale), tag(params.bn_bias),
@@ -43,8 +44,10 @@ class _WeightCache:
             w = params.weight.detach().to(device)
             scale, shift = folded_affine(spec, params)
             self.shift = None if shift is None else shift.to(device)
-            if precision == "split":
-                self.wp, pre = ops.pack_conv_weight_split(w, ops.pad16(spec.in_channels))
+            if precision in ("split", "planes"):
+                pack = (ops.pack_conv_weight_split if precision == "split"
+                        else ops.pack_conv_weight_planes)
+                self.wp, pre = pack(w, ops.pad16(spec.in_channels))
                 base = (torch.ones(spec.out_channels, dtype=torch.float32, device=device)
                         if scale is None else scale.to(device).float())
                 self.scale = (base / pre).contiguous()

@@ -34,6 +34,14 @@ class UnsupportedTopology(ValueError):
     pass
 
 
+# Network operand precision: "fp16" (fp16 weights, the reference GPU path's
+# operand precision: TF32 cuDNN / fp16 StreamFuse), "split" (hi + lo weights
+# and stem input everywhere) or "fp32" (fp32-faithful: the real-valued stem as
+# hi + lo, every spike layer that the channel-major kernel runs with exact
+# integer weight planes, the rest split).
+NETWORK_PRECISIONS = ("fp16", "split", "fp32")
+
+
 @dataclass
 class ConvStep:
     name: str
@@ -53,6 +61,7 @@ class ConvStep:
     stride: int = 0               # launch geometry (differs from spec for im2col)
     pad: int = 0
     im2col: bool = False
+    prec: str = "fp16"            # operand precision of this launch (ops.PRECISIONS)
 
 
 @dataclass
@@ -116,9 +125,10 @@ class NetworkPlan:
 
     def __init__(self, model: nn.Module, T: int, B: int, H: int, W: int, device,
                  use_sparse: bool = False, precision: str = "fp16"):
-        if precision not in ops.PRECISIONS:
-            raise ValueError(f"precision must be one of {ops.PRECISIONS}")
+        if precision not in NETWORK_PRECISIONS:
+            raise ValueError(f"precision must be one of {NETWORK_PRECISIONS}")
         self.precision = precision
+        hi_lo = precision != "fp16"   # real-valued stem input carried as hi + lo
         self.T, self.B, self.H, self.W = T, B, H, W
         self.device = torch.device(device)
         self.steps = []
@@ -131,9 +141,10 @@ class NetworkPlan:
         k0 = sspec.kernel_size
         # A stem with few input channels runs as a 1x1 convolution over an
         # im2col-packed input (one K chunk per tile instead of k*k taps).
-        # (split precision: hi and lo parts of the real-valued input side by side)
-        kk_mult = 2 if precision == "split" else 1
-        self.im2col = k0 > 1 and kk_mult * cin * k0 * k0 <= 64
+        # (hi + lo precision: the parts of the real-valued input side by side,
+        # for any kernel size)
+        kk_mult = 2 if hi_lo else 1
+        self.im2col = k0 > 1 and (hi_lo or cin * k0 * k0 <= 64)
         if self.im2col:
             ho0, wo0 = sspec.output_hw(H, W)
             self.shapes.append((B, ho0, wo0, T, ops.pad16(kk_mult * cin * k0 * k0)))
@@ -150,15 +161,22 @@ class NetworkPlan:
             self.shapes.append((b_, ho, wo, t_, spec.out_channels))
             dst = len(self.shapes) - 1
             sparse = use_sparse and isinstance(pat, STFusionConvBNLIF)
+            if precision == "fp16":
+                prec = "fp16"
+            elif precision == "fp32" and ops.planes_ok(spec.out_channels, c_):
+                prec, sparse = "planes", False   # the plane mode runs dense
+            else:
+                prec = "split"
             self.steps.append(ConvStep(name, nat, src, dst, identity, res_mode,
-                                       _lif_of(pat) if lif else None, sparse))
+                                       _lif_of(pat) if lif else None, sparse, prec=prec))
             return dst
 
         if self.im2col:
             b_, h_, w_, t_, c_ = self.shapes[0]
             self.shapes.append((b_, h_, w_, t_, sspec.out_channels))
             self.steps.append(ConvStep("stem", _native_of(stem), 0, 1, None, "none", _lif_of(stem),
-                                       False, stride=1, pad=0, im2col=True))
+                                       False, stride=1, pad=0, im2col=True,
+                                       prec="split" if hi_lo else "fp16"))
             cur = 1
         else:
             cur = add_conv("stem", stem, cur)
@@ -199,10 +217,10 @@ class NetworkPlan:
         self.acts = [torch.zeros(s, dtype=torch.float16, device=self.device) for s in self.shapes]
         for st in self.steps:
             if isinstance(st, ConvStep):
-                st.wp, st.scale, st.shift = st.native.packed(self.device, precision)
+                st.wp, st.scale, st.shift = st.native.packed(self.device, st.prec)
                 if st.im2col:
                     w0 = st.native.params.weight.detach().to(self.device)
-                    if precision == "split":
+                    if st.prec == "split":
                         st.wp, pre = ops.im2col_weight_split(w0, self.shapes[0][-1])
                         _, sc0, _ = st.native.packed(self.device, "fp16")
                         base = (torch.ones(w0.shape[0], dtype=torch.float32, device=self.device)
@@ -232,7 +250,7 @@ class NetworkPlan:
     def pack_input(self):
         if self.im2col:
             k, s_, p_ = self.stem_geom
-            pack = ops.pack_im2col_split if self.precision == "split" else ops.pack_im2col
+            pack = ops.pack_im2col_split if self.precision != "fp16" else ops.pack_im2col
             pack(self.x_in, k, s_, p_, self.shapes[0][-1], out=self.acts[0])
         else:
             ops.pack_tbchw(self.x_in, self.shapes[0][-1], out=self.acts[0])
@@ -253,14 +271,14 @@ class NetworkPlan:
             if st.lif is None:
                 ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
                                 st.pad, res_mode="z_only", out=self.acts[st.dst],
-                                precision=self.precision)
+                                precision=st.prec)
             else:
                 ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
                                 st.pad, identity=ident,
                                 res_mode=st.res_mode if ident is not None else "none",
                                 v_in=None if fresh else st.v, v_out=st.v,
                                 tile_mask=st.mask if st.sparse else None, lif=st.lif,
-                                out=self.acts[st.dst], precision=self.precision)
+                                out=self.acts[st.dst], precision=st.prec)
         ops.avgpool_fc(self.acts[self.final], self.fc_w, self.fc_b, out=self.logits)
 
     def run(self, use_graph: bool = True):
@@ -306,8 +324,8 @@ class CTFNetwork(nn.Module):
     def __init__(self, model: nn.Module, use_graph: bool = True, use_sparse: bool = False,
                  precision: str = "fp16"):
         super().__init__()
-        if precision not in ops.PRECISIONS:
-            raise ValueError(f"precision must be one of {ops.PRECISIONS}")
+        if precision not in NETWORK_PRECISIONS:
+            raise ValueError(f"precision must be one of {NETWORK_PRECISIONS}")
         self.model = model
         self.use_graph = use_graph
         self.use_sparse = use_sparse

@@ -27,8 +27,16 @@ __all__ = [
 
 # Operand precision of the fused conv: "fp16" = fp16 weights (spikes are exact
 # in fp16); "split" = weights (and a real-valued stem input) carried as fp16
-# hi + lo parts, two MMAs per chunk into the same fp32 accumulator.
-PRECISIONS = ("fp16", "split")
+# hi + lo parts, two MMAs per chunk into the same fp32 accumulator; "planes" =
+# weights quantised to 29-bit integers as three fp16 digit planes in separate
+# accumulators, exact accumulation for integer activations (spike counts).
+PRECISIONS = ("fp16", "split", "planes")
+WEIGHT_PARTS = {"fp16": 1, "split": 2, "planes": 3}
+
+
+def planes_ok(Cout: int, Cin_p: int) -> bool:
+    """The integer-plane mode runs on the channel-major kernel only."""
+    return Cout % 128 == 0 or (Cout % 64 == 0 and Cin_p >= 64)
 
 SPIKE_FORMATS = {torch.float32: FMT_F32, torch.float16: FMT_F16, torch.uint8: FMT_U8,
                  "bits": FMT_BITS}
@@ -325,6 +333,31 @@ def im2col_weight_split(w: torch.Tensor, Kp: Optional[int] = None):
     return pack_conv_weight_split(row.reshape(Cout, Kp, 1, 1), Kp)
 
 
+def planes_prescale(w: torch.Tensor) -> float:
+    """Power of two with max|w| * prescale in [2^27, 2^28)."""
+    m = float(w.detach().abs().max()) if w.numel() else 0.0
+    if m == 0.0 or m != m:
+        return 1.0
+    import math
+    e = math.frexp(m)[1]
+    return float(2.0 ** (28 - e))
+
+
+def pack_conv_weight_planes(w: torch.Tensor, Cin_p: Optional[int] = None,
+                            prescale: Optional[float] = None):
+    """w[Cout,Cin,KH,KW] -> (wq[Cout,KH,KW,3*Cin_p] fp16 digit planes, prescale):
+    q = rint(w * prescale) = q2 * 2^20 + q1 * 2^10 + q0, planes q2 | q1 | q0 per tap."""
+    w = w.detach().float().contiguous()
+    _need(w, "w", torch.float32)
+    Cout, Cin, KH, KW = w.shape
+    Cin_p = pad16(Cin) if Cin_p is None else int(Cin_p)
+    prescale = planes_prescale(w) if prescale is None else float(prescale)
+    out = torch.empty((Cout, KH, KW, 3 * Cin_p), dtype=torch.float16, device=w.device)
+    _lib.call("cf_pack_conv_weight_planes", w.data_ptr(), out.data_ptr(), Cout, Cin, KH, KW, Cin_p,
+              prescale, _stream())
+    return out, prescale
+
+
 def pack_conv_weight(w: torch.Tensor, Cin_p: Optional[int] = None):
     """w[Cout,Cin,KH,KW] -> [Cout,KH,KW,Cin_p] fp16 (zero padded)."""
     w = w.detach().float().contiguous()
@@ -340,12 +373,13 @@ def pack_conv_weight(w: torch.Tensor, Cin_p: Optional[int] = None):
 # fused conv / linear on tcgen05
 # ---------------------------------------------------------------------------
 
-def conv_geometry(T, B, Ho, Wo, Cout, Cin_p=64, stride=1, sparse=False):
+def conv_geometry(T, B, Ho, Wo, Cout, Cin_p=64, stride=1, sparse=False, planes=False):
     """Tile geometry cf_conv_bn_lif uses for this output shape and input width
     (the per-tile mask buffer of the sparse path has n_mtiles entries)."""
     import ctypes
     buf = (ctypes.c_int32 * 6)()
-    _lib.call("cf_conv_geometry_ex", T, B, Ho, Wo, Cout, Cin_p, stride, int(bool(sparse)), buf)
+    flags = (1 if sparse else 0) | (2 if planes else 0)
+    _lib.call("cf_conv_geometry_ex", T, B, Ho, Wo, Cout, Cin_p, stride, flags, buf)
     return dict(TP=buf[0], Wb=buf[1], Hb=buf[2], Bb=buf[3], n_mtiles=buf[4], BN=buf[5])
 
 
@@ -363,9 +397,10 @@ def conv_bn_lif(x: torch.Tensor, wp: torch.Tensor, scale: Optional[torch.Tensor]
                 tile_mask: Optional[torch.Tensor] = None, lif: LIFConfig = _DEFAULT_LIF,
                 out: Optional[torch.Tensor] = None, precision: str = "fp16"):
     """Fused conv+BN+LIF on x[B,H,W,T,Cin_p] fp16 with wp[Cout,KH,KW,Cin_p] fp16
-    (precision "fp16") or split weights wp[Cout,KH,KW,2*Cin_p] from
-    pack_conv_weight_split (precision "split"; scale already divided by the
-    prescale).
+    (precision "fp16"), split weights wp[Cout,KH,KW,2*Cin_p] from
+    pack_conv_weight_split (precision "split") or digit planes
+    wp[Cout,KH,KW,3*Cin_p] from pack_conv_weight_planes (precision "planes");
+    for the last two the scale is already divided by the prescale.
 
     Returns out[B,Ho,Wo,T,Cout] fp16.  v_out (if given) receives v_T in
     [B,Ho,Wo,Cout] fp32; v_in may alias v_out."""
@@ -375,7 +410,7 @@ def conv_bn_lif(x: torch.Tensor, wp: torch.Tensor, scale: Optional[torch.Tensor]
         raise ValueError(f"precision must be one of {PRECISIONS}")
     B, H, W, T, Cin_p = x.shape
     Cout, KH, KW, Cw = wp.shape
-    if Cw != (2 if precision == "split" else 1) * Cin_p:
+    if Cw != WEIGHT_PARTS[precision] * Cin_p:
         raise ValueError(f"weight channels {Cw} do not match activation Cin_p {Cin_p} "
                          f"at precision {precision!r}")
     Ho = (H + 2 * pad - KH) // stride + 1
@@ -399,6 +434,13 @@ def conv_bn_lif(x: torch.Tensor, wp: torch.Tensor, scale: Optional[torch.Tensor]
         out = torch.empty((B, Ho, Wo, T, Cout), dtype=torch.float16, device=x.device)
     else:
         _need(out, "out", torch.float16)
+    if precision == "planes":
+        if tile_mask is not None:
+            raise ValueError("the integer-plane mode runs dense only (no tile mask)")
+        _lib.call("cf_conv_bn_lif_planes", x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
+                  _ptr(identity), mode, _ptr(v_in), _ptr(v_out), out.data_ptr(),
+                  T, B, H, W, Cin_p, Cout, KH, KW, stride, pad, *lif.args(), _stream())
+        return out
     fn = "cf_conv_bn_lif_split" if precision == "split" else "cf_conv_bn_lif"
     _lib.call(fn, x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
               _ptr(identity), mode, _ptr(v_in), _ptr(v_out), out.data_ptr(), _ptr(tile_mask),

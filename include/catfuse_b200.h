@@ -148,11 +148,13 @@ CF_API int cf_pack_conv_weight(const float* w, void* wp, int64_t Cout, int64_t C
  * per-tile mask buffer.  out[0..5] = {Tp, Wb, Hb, Bb, n_mtiles, BN}.
  * cf_conv_geometry assumes Cin_p = 64, stride 1 and dense chunks; the tile
  * choice depends on Cin_p, so callers that know it use cf_conv_geometry_ex
- * (same output, the arguments cf_conv_bn_lif / cf_prescan_conv_tiles get). */
+ * (same output, the arguments cf_conv_bn_lif / cf_prescan_conv_tiles get).
+ * flags: bit 0 = sparse (tile-mask launch), bit 1 = integer weight planes
+ * (cf_conv_bn_lif_planes). */
 CF_API int cf_conv_geometry(int64_t T, int64_t B, int64_t Ho, int64_t Wo,
                      int64_t Cout, int32_t* out6);
 CF_API int cf_conv_geometry_ex(int64_t T, int64_t B, int64_t Ho, int64_t Wo, int64_t Cout,
-                               int64_t Cin_p, int64_t stride, int sparse, int32_t* out6);
+                               int64_t Cin_p, int64_t stride, int flags, int32_t* out6);
 
 /* Implicit-GEMM convolution on the 5th-generation tensor cores (fp16
  * operands, fp32 accumulation in TMEM) with the BN affine, the optional
@@ -277,6 +279,33 @@ CF_API int cf_pack_conv_weight_split(const float* w, void* wp2, int64_t Cout, in
 CF_API int cf_pack_im2col_split(const void* x, int x_fmt, void* y, int64_t T, int64_t B,
                                 int64_t C, int64_t H, int64_t W, int64_t k, int64_t stride,
                                 int64_t pad, int64_t Kp, void* stream);
+
+/* Exact-accumulation variant for integer activations (spike counts): the
+ * weight is quantised to q = rint(w * prescale), |q| < 2^28, and carried as
+ * three planes of signed base-1024 digits wq[Cout][KH][KW][3][Cin_p] fp16
+ * (cf_pack_conv_weight_planes; most significant plane first).  Each plane is
+ * accumulated in its own TMEM accumulator; with |x| <= 2^24 / (512*KH*KW*Cin_p)
+ * (e.g. |x| <= 7 at KH*KW*Cin_p = 4608) every partial sum is an integer below
+ * 2^24, so the accumulation is exact, and the epilogue joins the planes in
+ * fp64 and rounds once: conv = round_fp32(sum x * q), i.e. the convolution with
+ * the 29-bit quantised weight, correctly rounded.  `scale` is the BN scale
+ * divided by prescale.  Three MMAs per chunk, single-buffered N = 128 tiles;
+ * channel-major shapes only (Cout % 128 == 0, or Cout % 64 == 0 with
+ * Cin_p >= 64); dense only (no tile mask).  This is the fp32 reference path
+ * of DenseKeep (catfuse/implementations/dense_keep.py:97-155) made exact. */
+CF_API int cf_conv_bn_lif_planes(const void* x, const void* wq, const float* scale,
+                                 const float* shift, const void* identity, int res_mode,
+                                 const float* v_in, float* v_out, void* out,
+                                 int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin_p,
+                                 int64_t Cout, int64_t KH, int64_t KW, int64_t stride,
+                                 int64_t pad, float tau, float v_threshold, float v_reset,
+                                 int hard_reset, int decay_input, void* stream);
+/* w[Cout][Cin][KH][KW] fp32 -> wq[Cout][KH][KW][3][Cin_p] fp16 digit planes of
+ * q = rint(w * prescale) (see cf_conv_bn_lif_planes); prescale a power of two
+ * with max |w| * prescale < 2^28. */
+CF_API int cf_pack_conv_weight_planes(const float* w, void* wq, int64_t Cout, int64_t Cin,
+                                      int64_t KH, int64_t KW, int64_t Cin_p, float prescale,
+                                      void* stream);
 
 /* ---- bounded device-side waits ------------------------------------------- */
 

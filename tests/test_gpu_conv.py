@@ -341,3 +341,83 @@ def test_im2col_split_stem(dev, shape):
     _, _, h32 = lif_trace(z32)
     check_lif_parity(sg, vg, s32, v32, h32, v_tol=1e-4, near_tol=1e-4, max_flip_rate=1e-4,
                      what=f"split stem {shape}")
+
+
+PLANE_SHAPES = [
+    # B, Cin, Cout, H, W, k, stride, pad
+    (8, 64, 64, 32, 32, 3, 1, 1),      # M=64 channel-major tiles
+    (8, 128, 128, 16, 16, 3, 1, 1),    # kh-box stages
+    (4, 512, 512, 4, 4, 3, 1, 1),      # kw-group stages, K = 4608
+    (4, 64, 128, 16, 16, 3, 2, 1),     # stride 2
+    (4, 64, 128, 16, 16, 1, 2, 0),     # 1x1 downsample
+    (3, 96, 256, 9, 7, 3, 1, 1),       # ragged tiles, Cin_p not a multiple of 64
+]
+
+
+@pytest.mark.parametrize("shape", PLANE_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_conv_planes_exact_accumulation(dev, shape):
+    """Integer weight planes: the convolution equals the fp64 convolution with
+    the quantised weight q / prescale, rounded once to fp32 -- bit for bit.
+    Read through the membrane: T=1, v0=0, no spikes, so v = z / 2 exactly."""
+    ops = _ops()
+    B, Cin, Cout, H, W, k, st, pad = shape
+    g = torch.Generator().manual_seed(sum(shape))
+    x = ((torch.rand(1, B, Cin, H, W, generator=g) < 0.3).float()
+         + (torch.rand(1, B, Cin, H, W, generator=g) < 0.2).float())   # counts {0,1,2}
+    w = torch.randn(Cout, Cin, k, k, generator=g) * (2.0 / (Cin * k * k)) ** 0.5
+    xp = ops.pack_tbchw(x.to(dev))
+    wq, pre = ops.pack_conv_weight_planes(w.to(dev), xp.shape[-1])
+    # the planes reproduce q = rint(w * prescale) exactly
+    planes = wq.cpu().double().reshape(Cout, k, k, 3, -1)[..., :Cin]
+    q = planes[..., 0, :] * 2.0 ** 20 + planes[..., 1, :] * 2.0 ** 10 + planes[..., 2, :]
+    assert torch.equal(q, torch.round((w.double() * pre)).permute(0, 2, 3, 1))
+    assert planes.abs().max() <= 512
+    Ho = (H + 2 * pad - k) // st + 1
+    Wo = (W + 2 * pad - k) // st + 1
+    v = torch.empty(B, Ho, Wo, Cout, device=dev)
+    lif = ops.LIFConfig(2.0, 1e30, 0.0, True)
+    sc = torch.full((Cout,), 1.0 / pre, device=dev)
+    ops.conv_bn_lif(xp, wq, sc, torch.zeros(Cout, device=dev), st, pad, v_out=v, lif=lif,
+                    precision="planes")
+    z = (ops.v_to_nchw(v).cpu() * 2).double()
+    qw = q.permute(0, 3, 1, 2) / pre
+    z64 = torch.nn.functional.conv2d(x[0].double(), qw, stride=st, padding=pad)
+    assert torch.equal(z, z64.float().double())
+
+
+@pytest.mark.parametrize("shape", [(4, 4, 128, 128, 16, 16, 3, 1, 1), (4, 2, 64, 64, 32, 32, 3, 1, 1),
+                                   (12, 1, 64, 128, 6, 6, 3, 1, 1)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("mode", ["none", "add", "add_pre"])
+def test_conv_planes_vs_fp32_oracle(dev, shape, mode):
+    """Full Conv->BN->LIF in the plane mode (residual modes, chunked T) at the
+    fp32 tolerance: v within 1e-4, flips only within 1e-5 of the threshold."""
+    ops = _ops()
+    T, B, Cin, Cout, H, W, k, st, pad = shape
+    x, w, scale, shift = _case(T, B, Cin, Cout, H, W, k, seed=sum(shape) + len(mode))
+    g = torch.Generator().manual_seed(3)
+    xp = ops.pack_tbchw(x.to(dev))
+    wq, pre = ops.pack_conv_weight_planes(w.to(dev), xp.shape[-1])
+    kw = {}
+    ident = None
+    if mode != "none":
+        ident = (torch.rand(T, B, Cout, H, W, generator=g) < 0.3).float()
+        kw = dict(identity=ops.pack_tbchw(ident.to(dev)), res_mode=mode)
+    v = torch.empty(B, H, W, Cout, device=dev)
+    out = ops.conv_bn_lif(xp, wq, (scale / pre).to(dev), shift.to(dev), st, pad, v_out=v,
+                          precision="planes", **kw)
+    got = ops.unpack_bhwtc(out).cpu().numpy()
+    vg = ops.v_to_nchw(v).cpu().numpy()
+    if mode == "none":
+        s32, v32, z32 = oracle.conv_bn_lif(x, w, scale, shift, st, pad, return_z=True)
+        ref = s32
+    else:
+        ref, v32 = oracle.conv_bn_lif_residual(x, w, scale, shift, ident, mode, st, pad)
+        z32 = oracle.conv.conv_z(x, w, scale, shift, st, pad).numpy()
+        if mode == "add_pre":
+            z32 = (z32 + ident.numpy()).astype(np.float32)
+        got = got - ident.numpy() if mode == "add" else got
+        ref = ref - ident.numpy() if mode == "add" else ref
+    _, _, h32 = lif_trace(z32)
+    check_lif_parity(got, vg, ref, v32, h32, v_tol=1e-4, near_tol=1e-5, max_flip_rate=1e-4,
+                     what=f"planes {mode} {shape}")
