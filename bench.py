@@ -11,7 +11,8 @@ logits are all-gathered over NCCL at the end of each step.
 
 ``value``: samples/s of the whole job with inputs resident in HBM (the
 forward is one CUDA-graph replay of fused sm_100a kernels), each step timed
-with CUDA events, L2 flushed (256 MB write) between steps outside the timed
+with CUDA events, L2 flushed (256 MB write, then a 256 MB read so no dirty line
+is left) between steps outside the timed
 events, max over ranks.  ``e2e``: the same metric through the public API
 (``optimize``'d model called on a device copy of pinned host images, logits
 read back to the host), host<->device copies inside the timed region.
@@ -35,11 +36,12 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from catfuse_b200.timing import L2Flush  # noqa: E402
+
 METRIC = "SEW-ResNet18 T=4 samples/s"
 UNIT = "samples/s"
 T_STEPS = 4
 BATCH = 64
-L2_FLUSH_BYTES = 256 << 20
 
 
 def _peaks():
@@ -164,7 +166,7 @@ def time_plan(plan, steps, flush, dist=None, gathered=None):
         dist.barrier()
     torch.cuda.synchronize()
     for s, e in evs:
-        flush.fill_(1.0)
+        flush()
         s.record()
         step()
         e.record()
@@ -234,6 +236,27 @@ def run_reference(args):
     return 0
 
 
+def egd_report(plan):
+    """Device-side EGD of the STFusion sites in the last forward: the active
+    (tile, chunk) fraction of each site's prescan masks and what the kernel
+    chose with the profile's threshold."""
+    from catfuse_b200 import ops
+    from catfuse_b200.network import ConvStep
+    out = {}
+    for st in plan.steps:
+        if not isinstance(st, ConvStep) or not st.sparse:
+            continue
+        cin_p = plan.shapes[st.src][-1]
+        n_kx = cin_p // ops.conv_chunk(cin_p, False)   # device-dispatch masks: dense chunk
+        bits = (1 << n_kx) - 1
+        masks = st.mask.cpu().tolist()
+        active = sum(bin(int(m) & bits).count("1") for m in masks) / (len(masks) * n_kx)
+        choice = ("StaticZero" if active == 0 else
+                  ("SparseFlow" if active <= plan.egd_frac else "DenseKeep"))
+        out[st.name] = {"active_frac": round(active, 4), "decision": choice}
+    return {"max_active_frac": plan.egd_frac, "sites": out} if out else None
+
+
 def conv_roofline(plan, flush, peaks, peak_src):
     """The forward's conv launches replayed alone as one CUDA graph (same
     inputs, same order, L2 flushed before each replay), plus each launch timed
@@ -266,7 +289,7 @@ def conv_roofline(plan, flush, peaks, peak_src):
     torch.cuda.synchronize()
     conv_ms = []
     for _ in range(5):
-        flush.fill_(1.0)
+        flush()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
@@ -281,17 +304,22 @@ def conv_roofline(plan, flush, peaks, peak_src):
         b_, ho, wo, t_, co = plan.shapes[st.dst]
         spec = st.native.spec
         fl = 2.0 * t_ * b_ * ho * wo * co * spec.in_channels * spec.kernel_size ** 2
+        g1 = torch.cuda.CUDAGraph()          # one launch, replayed (no host overhead timed)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(g1, stream=side):
+            launch(st)
+        torch.cuda.synchronize()
         ts = []
-        for _ in range(5):
-            flush.fill_(1.0)
+        for _ in range(20):   # mean of 20: the event clock ticks in ~4 us steps here
+            flush()
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record()
-            launch(st)
+            g1.replay()
             b.record()
-            torch.cuda.synchronize()
-            ts.append(a.elapsed_time(b))
-        us = 1000.0 * statistics.median(ts)
+            ts.append((a, b))
+        torch.cuda.synchronize()
+        us = 1000.0 * statistics.mean(a.elapsed_time(b) for a, b in ts)
         per_layer.append({"layer": st.name, "us": round(us, 2),
                           "tflops": round(fl / us / 1e6, 1),
                           "frac": round(fl / us / 1e6 / peak, 3)})
@@ -339,7 +367,7 @@ def main():
     x_dev = images.to(dev).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1).contiguous()
     plan = model.plan_for(x_dev)
     plan.x_in.copy_(x_dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(dev)
     gathered = torch.empty((world, T_STEPS, B, 10), device=dev) if world > 1 else None
 
     for _ in range(args.warmup):
@@ -358,6 +386,7 @@ def main():
     ms_per_step = total_ms / args.steps
     value = world * B * args.steps / (total_ms / 1000.0)
 
+    egd = egd_report(plan)
     peaks, peak_src = _peaks()
     roofline = conv_roofline(plan, flush, peaks, peak_src)
     roofline["share_of_step"] = roofline["conv_ms_per_forward"] / ms_per_step
@@ -433,7 +462,7 @@ def main():
             "config": {"workload": "SEW-ResNet18 CIFAR T=4 forward (BASELINE config 1)",
                        "model": "sew_resnet18_cifar", "global_batch": world * B,
                        "per_gpu_batch": B, "seq_len": T_STEPS, "parallelism": f"dp{world}",
-                       "l2": "flushed (256 MB write) between timed steps",
+                       "l2": "flushed between timed steps (256 MB write, then 256 MB read)",
                        "weights": "random init (seed 0), BN statistics calibrated on synthetic data",
                        "operands": "fp16 spikes/weights, fp32 accumulate + LIF",
                        "precision": "fp16"},
@@ -444,6 +473,7 @@ def main():
                     "d2h_bytes_per_step": out_host.numel() * 4},
             "clocks": clocks,
             "routing": {k: v for k, v in stats["patterns_matched"].items()},
+            "egd": egd,
         }
         line.update(extras)
         if not args.no_cpu_baseline and world == 1:

@@ -38,7 +38,10 @@ def optimize(model, device="cuda:0", policy=None, T=16, use_sparseflow=True, nat
     if native:
         from .network import CTFNetwork, UnsupportedTopology
         try:
-            net = CTFNetwork(new_model, use_graph=use_graph, precision=precision)
+            # STFusion sites keep their runtime dispatch inside the native plan:
+            # prescan + device-side EGD (SparseFlow / DenseKeep / StaticZero)
+            net = CTFNetwork(new_model, use_graph=use_graph, use_sparse=use_sparseflow,
+                             precision=precision)
             stats["native_plan"] = True
             return net, stats
         except UnsupportedTopology as e:

@@ -202,7 +202,8 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
                      void* out, const uint32_t* tile_mask, int64_t T, int64_t B, int64_t H,
                      int64_t W, int64_t Cin_p, int64_t Cout, int64_t KH, int64_t KW,
                      int64_t stride, int64_t pad, float tau, float v_th, float v_reset,
-                     int hard_reset, int decay_input, int wparts, cudaStream_t stream) {
+                     int hard_reset, int decay_input, int wparts, cudaStream_t stream,
+                     float egd_max_active_frac = -1.f) {
   if (!x || !wp || !out) return fail(CF_ERR_INVALID_ARG, "x, wp and out must not be NULL");
   if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin_p <= 0 || Cout <= 0 || KH <= 0 || KW <= 0 ||
       stride <= 0 || pad < 0)
@@ -231,7 +232,11 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   const int nplanes = wparts == 3 ? 3 : 1;
   if (nplanes > 1 && tile_mask)
     return fail(CF_ERR_UNSUPPORTED, "integer weight planes run dense only (no tile mask)");
-  if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, tile_mask != nullptr, g, nplanes))
+  // Device-EGD launches use the dense channel chunk (their masks come from a
+  // prescan with that chunk); the tile boxes do not depend on the chunk.
+  const bool egd_launch = tile_mask && egd_max_active_frac >= 0.f;
+  if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, tile_mask != nullptr && !egd_launch,
+                             g, nplanes))
     return rc;
   const int n_kx = g.n_kc;  // activation chunks per tap
   g.n_kc *= wparts;          // weight chunks: part 0 chunks, then part 1, ...
@@ -338,6 +343,12 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.err = dev_error_ptr();
   if (!args.err) return fail(CF_ERR_CUDA, "device error word is not addressable");
   args.drop_load = g_stall_armed.exchange(0) ? 1 : 0;
+  args.egd = (tile_mask && egd_max_active_frac >= 0.f) ? 1 : 0;
+  if (args.egd) {
+    const double pairs = (double)g.n_mtiles * n_kx;
+    const double lim = egd_max_active_frac >= 1.f ? pairs : floor(egd_max_active_frac * pairs);
+    args.egd_max_active = (uint32_t)(lim > 4294967295.0 ? 4294967295.0 : lim);
+  }
   args.stages = 0;
   args.wres = wres;
   args.halo = halo;
@@ -454,6 +465,20 @@ int cf_conv_bn_lif_split(const void* x, const void* wp2, const float* scale, con
   return conv_bn_lif_impl(x, wp2, scale, shift, identity, res_mode, v_in, v_out, out, tile_mask, T,
                           B, H, W, Cin_p, Cout, KH, KW, stride, pad, tau, v_threshold, v_reset,
                           hard_reset, decay_input, 2, static_cast<cudaStream_t>(stream));
+}
+
+int cf_conv_bn_lif_egd(const void* x, const void* wp, const float* scale, const float* shift,
+                       const void* identity, int res_mode, const float* v_in, float* v_out,
+                       void* out, const uint32_t* tile_mask, int64_t T, int64_t B, int64_t H,
+                       int64_t W, int64_t Cin_p, int64_t Cout, int64_t KH, int64_t KW,
+                       int64_t stride, int64_t pad, float tau, float v_threshold, float v_reset,
+                       int hard_reset, int decay_input, float max_active_frac, void* stream) {
+  if (!tile_mask) return fail(CF_ERR_INVALID_ARG, "the device dispatch needs the tile masks");
+  if (!(max_active_frac >= 0.f)) return fail(CF_ERR_INVALID_ARG, "max_active_frac must be >= 0");
+  return conv_bn_lif_impl(x, wp, scale, shift, identity, res_mode, v_in, v_out, out, tile_mask, T,
+                          B, H, W, Cin_p, Cout, KH, KW, stride, pad, tau, v_threshold, v_reset,
+                          hard_reset, decay_input, 1, static_cast<cudaStream_t>(stream),
+                          max_active_frac);
 }
 
 int cf_conv_bn_lif_planes(const void* x, const void* wq, const float* scale, const float* shift,

@@ -92,6 +92,8 @@ struct ConvArgs {
   uint32_t max_polls;  // bounded-wait limit (mbarrier polls before a wait gives up)
   int32_t* err;     // device error word (site code of the first expired wait)
   int drop_load;    // test hook: CTA 0's producers skip the first load (the wait for it expires)
+  int egd;          // 1: decide on the device whether the tile masks are used (egd_count_active)
+  uint32_t egd_max_active;  // most active (tile, chunk) pairs for which the masks run
   int nprod;        // producer threads in use (<= stages)
   int wres;         // 1: the whole weight slab of the (single) N tile stays in shared memory
   int halo;         // 1: one TMA box per tile carries the whole receptive field (all taps)
@@ -150,12 +152,27 @@ __device__ __forceinline__ bool warp_wait_or_abort(uint64_t* bar, uint32_t parit
 // weights walk wparts * n_kx chunks (part 0, then part 1, ...) over the same
 // activation chunks, so an activation chunk mask is repeated for every part.
 // Sparse launches have at most 32 chunks; dense ones may have more (chunk_on).
-__device__ __forceinline__ uint32_t tile_kmask(const ConvArgs& a, int mt) {
-  if (!a.tile_mask) return a.kc_all;
+__device__ __forceinline__ uint32_t tile_kmask(const ConvArgs& a, int mt, bool use_mask) {
+  if (!a.tile_mask || !use_mask) return a.kc_all;
   const uint32_t m = __ldg(a.tile_mask + mt);
   uint32_t r = m;
   for (int p = 1; p < a.wparts; ++p) r |= m << (p * a.n_kx);
   return r & a.kc_all;
+}
+
+// Execution-grounded dispatch on the device (egd launches): every CTA sums
+// the popcounts of all tile masks (active (tile, chunk) pairs) before the
+// pipeline starts and runs the masks only if at most egd_max_active pairs are
+// active; otherwise every tile runs every chunk (dense).  Both choices give
+// the same result bit for bit (skipped chunks add exact zeros); only the
+// speed differs.  `s_active` is the CTA's shared counter, zeroed by the caller.
+__device__ __forceinline__ void egd_count_active(const ConvArgs& a, unsigned int* s_active) {
+  const uint32_t kx_all = a.n_kx >= 32 ? 0xFFFFFFFFu : ((1u << a.n_kx) - 1u);
+  unsigned int c = 0;
+  for (int i = threadIdx.x; i < a.n_mtiles; i += blockDim.x)
+    c += __popc(__ldg(a.tile_mask + i) & kx_all);
+  for (int off = 16; off; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(s_active, c);
 }
 
 __device__ __forceinline__ bool chunk_on(uint32_t km, int kc) {
@@ -337,6 +354,14 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  // EGD counter: the word after the abort flag (a static __shared__ variable
+  // would come out of the 227 KB the dynamic allocation already claims)
+  unsigned int* s_active = reinterpret_cast<unsigned int*>(const_cast<int*>(abort_flag) + 1);
+  if (a.egd) {
+    if (threadIdx.x == 0) *s_active = 0;
+    __syncthreads();
+    egd_count_active(a, s_active);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -363,6 +388,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const bool use_mask = !a.egd || *s_active <= a.egd_max_active;
 
   if (warp < kProdWarps) {
     // ------------------------------------------------------------ producers
@@ -398,7 +424,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int wi0 = wt * a.Wb * a.stride - a.pad;
         const int hi0 = ht * a.Hb * a.stride - a.pad;
         const int b0 = bt * a.Bb;
-        const uint32_t km = tile_kmask(a, mt);
+        const uint32_t km = tile_kmask(a, mt, use_mask);
         if (km == 0) continue;
         int tap = 0;
         for (int kh = 0; kh < KHs && ok; ++kh) {
@@ -477,7 +503,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       bool w_ready = false;
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int mt = tile / a.n_ntiles;
-        const uint32_t km = tile_kmask(a, mt);
+        const uint32_t km = tile_kmask(a, mt, use_mask);
         if (!wait_or_abort(&tempty_bar[acc], acc_phase ^ 1u, ERR_SITE_MMA_TEMPTY, abort_flag, a)) {
           ok = false;
           break;
@@ -577,7 +603,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const int wt = mt % a.n_wt;
       const int ht = (mt / a.n_wt) % a.n_ht;
       const int bt = mt / (a.n_wt * a.n_ht);
-      const bool has_acc = tile_kmask(a, mt) != 0;
+      const bool has_acc = tile_kmask(a, mt, use_mask) != 0;
       // The whole warp waits for the accumulator (backed off, converged).
       if (!warp_wait_or_abort(&tfull_bar[acc], acc_phase, ERR_SITE_EPI_TFULL, abort_flag,
                               a, a.backoff))
@@ -906,6 +932,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  // EGD counter: the word after the abort flag (a static __shared__ variable
+  // would come out of the 227 KB the dynamic allocation already claims)
+  unsigned int* s_active = reinterpret_cast<unsigned int*>(const_cast<int*>(abort_flag) + 1);
+  if (a.egd) {
+    if (threadIdx.x == 0) *s_active = 0;
+    __syncthreads();
+    egd_count_active(a, s_active);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -931,6 +965,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const bool use_mask = !a.egd || *s_active <= a.egd_max_active;
 
   if (warp < kProdWarps) {
     // ------------------------------------------------------------ producers
@@ -952,7 +987,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         const int wi0 = wt * a.Wb * a.stride - a.pad;
         const int hi0 = ht * a.Hb * a.stride - a.pad;
         const int b0 = bt * a.Bb;
-        const uint32_t km = tile_kmask(a, pt);
+        const uint32_t km = tile_kmask(a, pt, use_mask);
         if (km == 0) continue;
         for (int gh = 0; gh < n_gh && ok; ++gh) {
           for (int gw = 0; gw < n_gw && ok; ++gw) {
@@ -1031,7 +1066,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < a.n_tiles && ok; tile += gridDim.x) {
         const int pt = tile / n_ct;
-        const uint32_t km = tile_kmask(a, pt);
+        const uint32_t km = tile_kmask(a, pt, use_mask);
         if (!wait_or_abort(&tempty_bar[acc], acc_phase ^ 1u, ERR_SITE_MMA_TEMPTY, abort_flag, a)) {
           ok = false;
           break;
@@ -1117,7 +1152,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
       const int wt = pt % a.n_wt;
       const int ht = (pt / a.n_wt) % a.n_ht;
       const int bt = pt / (a.n_wt * a.n_ht);
-      const bool has_acc = tile_kmask(a, pt) != 0;
+      const bool has_acc = tile_kmask(a, pt, use_mask) != 0;
       const int co_base = ct * MT + q * (MT / 4);
       const int co = co_base + (MT == 128 ? lane : (lane & 15));
       const float sc = a.scale ? __ldg(a.scale + co) : 1.f;

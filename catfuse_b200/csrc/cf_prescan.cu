@@ -2,16 +2,16 @@
 //
 // cf_prescan: the reference geometry.  For output tile (n, gh, gw) of size
 // BH x BW, bit g of ag_mask is set iff some |x| > threshold lies in channel
-// group g inside the receptive field of the tile's valid output pixels —
+// group g inside the receptive field of the tile's valid output pixels --
 // the semantics of the reference's max-pool cascade (abs-amax per channel
-// group -> max_pool(k, s, p) -> max_pool(tile, ceil) -> > threshold).  One
-// CTA per tile; the CTA's warps stride over the receptive field, coalesced
-// along W, and combine their per-thread group masks with warp ballots and a
-// shared-memory OR.
+// group -> max_pool(k, s, p) -> max_pool(tile, ceil) -> > threshold).  Every
+// input element is read once (see prescan_ref_kernel).
 //
 // cf_prescan_conv_tiles: the fused conv kernel's own M-tile geometry over the
-// [B][H][W][T][Cin_p] fp16 activations, one 16-byte vector per thread step.
+// [B][H][W][T][Cin_p] fp16 activations, one pass (every element read once).
 #include "cf_common.cuh"
+
+#include <atomic>
 
 namespace cf {
 
@@ -29,221 +29,325 @@ __device__ __forceinline__ float load_any(const void* p, int fmt, int64_t i) {
   return (float)static_cast<const uint8_t*>(p)[i];
 }
 
-// Does input row `i` feed some output row in [o0, o1] (inclusive) of a
-// (k, s, p) convolution?
-__device__ __forceinline__ bool feeds(int i, int o0, int o1, int k, int s, int p) {
-  // outputs o with 0 <= i + p - o*s < k
-  const int num_hi = i + p;          // o*s <= i + p
-  const int num_lo = i + p - k + 1;  // o*s >= i + p - k + 1
-  int omax = num_hi >= 0 ? num_hi / s : -1;
-  int omin = num_lo <= 0 ? 0 : (num_lo + s - 1) / s;
-  if (omin < o0) omin = o0;
-  if (omax > o1) omax = o1;
-  return omin <= omax;
-}
+// Reference-geometry prescan, one pass over x[N][C][H][W]: CTA (n, channel
+// block) streams the block's H*W planes (thread = pixel, coalesced along the
+// plane, eight channels' loads in flight), ORs each pixel's group bits
+// together over its channels, then ORs them into the shared masks of every
+// tile whose valid output pixels' receptive fields contain the pixel (row and
+// column -> tile-range tables), and flushes the sample's masks with
+// atomicOr into the zeroed ag_mask.  The tile classes follow in
+// prescan_classify_kernel once every channel block has been merged.
+constexpr int kMaxTilesPerSample = 8192;
+constexpr int kRefChannelsPerCta = 32;
 
 __global__ void __launch_bounds__(kPrescanThreads)
     prescan_ref_kernel(const void* __restrict__ x, int fmt, int32_t* __restrict__ ag_mask,
-                       int32_t* __restrict__ tile_class, int C, int H, int W, int H_out,
-                       int W_out, int k, int s, int p, int BH, int BW, int GS, int G, int GH,
-                       int GW, float thr) {
-  __shared__ uint32_t s_mask;
-  const int tile = blockIdx.x;
-  const int gw = tile % GW;
-  const int gh = (tile / GW) % GH;
-  const int n = tile / (GW * GH);
-  const int o_h0 = gh * BH, o_h1 = min(H_out, o_h0 + BH) - 1;
-  const int o_w0 = gw * BW, o_w1 = min(W_out, o_w0 + BW) - 1;
-  const int r0 = max(0, o_h0 * s - p), r1 = min(H, o_h1 * s - p + k);
-  const int c0 = max(0, o_w0 * s - p), c1 = min(W, o_w1 * s - p + k);
-  const int rh = max(0, r1 - r0), rw = max(0, c1 - c0);
-  if (threadIdx.x == 0) s_mask = 0;
+                       int64_t* nnz, int C, int H, int W, int H_out, int W_out, int k, int s,
+                       int p, int BH, int BW, int GS, int GH, int GW, float thr) {
+  extern __shared__ uint32_t s_tiles[];           // GH * GW masks of this sample
+  uint16_t* s_row = reinterpret_cast<uint16_t*>(s_tiles + GH * GW);  // (first tile, count)
+  uint16_t* s_col = s_row + 2 * H;
+  __shared__ unsigned long long s_cnt;
+  const int n_cb = (C + kRefChannelsPerCta - 1) / kRefChannelsPerCta;
+  const int n = blockIdx.x / n_cb;
+  const int cb = blockIdx.x - n * n_cb;
+  const int c0 = cb * kRefChannelsPerCta, c1 = min(C, c0 + kRefChannelsPerCta);
+  for (int i = threadIdx.x; i < GH * GW; i += blockDim.x) s_tiles[i] = 0;
+  if (threadIdx.x == 0) s_cnt = 0;
+  // input row ih feeds output rows o with o*s in [ih + p - k + 1, ih + p],
+  // o < H_out; tile rows o / BH of that range
+  for (int i = threadIdx.x; i < H + W; i += blockDim.x) {
+    const bool is_row = i < H;
+    const int pos = is_row ? i : i - H;
+    const int n_out = is_row ? H_out : W_out, tb = is_row ? BH : BW;
+    int olo = pos + p - k + 1, ohi = pos + p;
+    olo = olo <= 0 ? 0 : (olo + s - 1) / s;
+    ohi = ohi < 0 ? -1 : min(n_out - 1, ohi / s);
+    uint16_t first = 0, cntt = 0;
+    if (olo <= ohi) {
+      first = (uint16_t)(olo / tb);
+      cntt = (uint16_t)(ohi / tb - olo / tb + 1);
+    }
+    uint16_t* dst = is_row ? s_row + 2 * pos : s_col + 2 * pos;
+    dst[0] = first;
+    dst[1] = cntt;
+  }
   __syncthreads();
-  uint32_t m = 0;
   const int64_t plane = (int64_t)H * W;
-  const int64_t base = (int64_t)n * C * plane;
-  // Thread -> fixed receptive-field position (row, col), channels strided by
-  // the number of threads that share a position: divisions and the "does it
-  // feed an output of the tile" test run once per position, not per element.
-  const int P = rh * rw;
-  if (P > 0) {
-    // P <= blockDim: nrep threads share each position (channels strided by
-    // nrep); otherwise each thread walks positions tid, tid + blockDim, ...
-    const bool rep = (int)blockDim.x >= P;
-    const int nrep = rep ? (int)blockDim.x / P : 1;
-    const int pos_step = rep ? P : (int)blockDim.x;
-    const int tid = threadIdx.x;
-    if (tid < (rep ? nrep * P : (int)blockDim.x)) {
-      const int c_first = rep ? tid / P : 0;
-      for (int pos = rep ? tid % P : tid; pos < P; pos += pos_step) {
-        const int row = pos / rw, col = pos - (pos / rw) * rw;
-        const int ih = r0 + row, iw = c0 + col;
-        if (feeds(ih, o_h0, o_h1, k, s, p) && feeds(iw, o_w0, o_w1, k, s, p)) {
-          const int64_t off = base + (int64_t)ih * W + iw;
-          // four channels' loads in flight together, then the group bits
-          for (int c = c_first; c < C; c += 4 * nrep) {
-            float v4[4];
+  const int64_t base = ((int64_t)n * C + c0) * plane;
+  const bool count = nnz != nullptr;
+  unsigned long long cnt = 0;
+  // Thread -> group of 8 consecutive pixels of the plane (one 16-byte fp16
+  // load, two fp32 loads or one 8-byte u8 load per channel when the plane
+  // allows it), four channels' loads in flight.
+  const int HW = H * W;
+  const int esz = fmt == CF_FMT_F32 ? 4 : (fmt == CF_FMT_F16 ? 2 : 1);
+  const bool vec = (HW % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(x) + (uintptr_t)(base * esz)) % 16 == 0);
+  const int ngrp = vec ? HW / 8 : HW;
+  const __half2 thr2 = __half2half2(__float2half_rd(thr));  // |h| > thr  <=>  |h| > rd_half(thr)
+  for (int grp = threadIdx.x; grp < ngrp; grp += blockDim.x) {
+    const int px0 = vec ? grp * 8 : grp;
+    const int npx = vec ? 8 : 1;
+    uint32_t bits[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    // nonzero-pixel mask of the current channel group, folded into bits[]
+    // when the group changes (group bits are per GS channels)
+    int g_cur = c0 / GS;
+    uint32_t nzpix = 0;
+    auto fold = [&]() {
+      if (!nzpix) return;
+      const uint32_t gbit = 1u << g_cur;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int cu = c + u * nrep;
-              v4[u] = cu < C ? load_any(x, fmt, off + cu * plane) : 0.f;
-            }
+      for (int j = 0; j < 8; ++j) bits[j] |= ((nzpix >> j) & 1u) ? gbit : 0u;
+      nzpix = 0;
+    };
+    for (int c = c0; c < c1; c += 4) {
+      uint32_t nzf[4];  // bit j: pixel px0 + j of channel c + u has |x| > thr
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (c + u * nrep < C && fabsf(v4[u]) > thr) m |= 1u << ((c + u * nrep) / GS);
+      for (int u = 0; u < 4; ++u) {
+        nzf[u] = 0u;
+        if (c + u >= c1) continue;
+        const int64_t e0 = base + (int64_t)(c + u - c0) * plane + px0;
+        if (vec && fmt == CF_FMT_F16) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(x) + e0));
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const unsigned gt = __hgt2_mask(__habs2(*reinterpret_cast<const __half2*>(&w[k])), thr2);
+            nzf[u] |= ((gt & 1u) | ((gt >> 15) & 2u)) << (2 * k);
+            if (count) cnt += ((w[k] & 0x7FFFu) != 0) + ((w[k] & 0x7FFF0000u) != 0);
           }
+        } else if (vec) {
+          float f[8];
+          if (fmt == CF_FMT_F32) {
+            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) + e0);
+            const float4 a = __ldg(src), b = __ldg(src + 1);
+            f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+            f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+          } else {
+            const uint2 q = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(x) + e0));
+            const uint8_t* b8 = reinterpret_cast<const uint8_t*>(&q);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = (float)b8[j];
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            nzf[u] |= (fabsf(f[j]) > thr ? 1u : 0u) << j;
+            if (count) cnt += f[j] != 0.f ? 1ull : 0ull;
+          }
+        } else {
+          const float f = load_any(x, fmt, e0);
+          nzf[u] = fabsf(f) > thr ? 1u : 0u;
+          if (count) cnt += f != 0.f ? 1ull : 0ull;
         }
       }
-    }
-  }
-  // warp-level OR, then one shared atomic per warp
-  for (int off = 16; off; off >>= 1) m |= __shfl_xor_sync(0xffffffffu, m, off);
-  if ((threadIdx.x & 31) == 0 && m) atomicOr(&s_mask, m);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t all = (G >= 32) ? 0xFFFFFFFFu : ((1u << G) - 1u);
-    const uint32_t mk = s_mask;
-    ag_mask[tile] = (int32_t)mk;
-    tile_class[tile] = (mk == 0) ? 0 : (mk == all ? 2 : 1);
-  }
-}
-
-// Count nonzero elements (any format), grid-stride, one atomic per block.
-__global__ void __launch_bounds__(kPrescanThreads)
-    count_nonzero_kernel(const void* __restrict__ x, int fmt, int64_t n, int64_t* nnz) {
-  __shared__ unsigned long long s_cnt;
-  if (threadIdx.x == 0) s_cnt = 0;
-  __syncthreads();
-  unsigned long long c = 0;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  int64_t head = 0;
-  if (fmt == CF_FMT_F16 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    // 8 halves per 16-byte load; the scalar loop below takes the tail
-    const int64_t nv = n / 8;
-    const uint4* xv = static_cast<const uint4*>(x);
-    for (int64_t i = first; i < nv; i += stride) {
-      const uint4 u = __ldg(xv + i);
-      const uint32_t w4[4] = {u.x & 0x7FFF7FFFu, u.y & 0x7FFF7FFFu, u.z & 0x7FFF7FFFu,
-                              u.w & 0x7FFF7FFFu};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) c += ((w4[j] & 0xFFFFu) != 0) + ((w4[j] >> 16) != 0);
+      for (int u = 0; u < 4; ++u) {
+        if (c + u >= c1) continue;
+        const int g = (c + u) / GS;
+        if (g != g_cur) {
+          fold();
+          g_cur = g;
+        }
+        nzpix |= nzf[u];
+      }
     }
-    head = nv * 8;
+    fold();
+    for (int j = 0; j < npx; ++j) {
+      if (!bits[j]) continue;
+      const int pix = px0 + j;
+      const int ih = pix / W, iw = pix - (pix / W) * W;
+      const int tr0 = s_row[2 * ih], nr = s_row[2 * ih + 1];
+      const int tc0 = s_col[2 * iw], nc = s_col[2 * iw + 1];
+      for (int a = 0; a < nr; ++a)
+        for (int b = 0; b < nc; ++b) atomicOr(&s_tiles[(tr0 + a) * GW + tc0 + b], bits[j]);
+    }
   }
-  for (int64_t i = head + first; i < n; i += stride)
-    c += (load_any(x, fmt, i) != 0.f) ? 1ull : 0ull;
-  for (int off = 16; off; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
-  if ((threadIdx.x & 31) == 0 && c) atomicAdd(&s_cnt, c);
+  if (count) {
+    for (int off = 16; off; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+    if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&s_cnt, cnt);
+  }
   __syncthreads();
-  if (threadIdx.x == 0 && s_cnt) atomicAdd(reinterpret_cast<unsigned long long*>(nnz), s_cnt);
+  int32_t* dst = ag_mask + (int64_t)n * GH * GW;
+  for (int i = threadIdx.x; i < GH * GW; i += blockDim.x)
+    if (s_tiles[i]) atomicOr(reinterpret_cast<unsigned int*>(dst + i), s_tiles[i]);
+  if (threadIdx.x == 0 && count && s_cnt)
+    atomicAdd(reinterpret_cast<unsigned long long*>(nnz), s_cnt);
 }
 
-// Conv-tile prescan over x[B][H][W][T][Cin_p] fp16.
+__global__ void prescan_classify_kernel(const int32_t* __restrict__ ag_mask,
+                                        int32_t* __restrict__ tile_class, int64_t tiles, int G) {
+  const uint32_t all = (G >= 32) ? 0xFFFFFFFFu : ((1u << G) - 1u);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tiles;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t mk = (uint32_t)ag_mask[i];
+    tile_class[i] = (mk == 0) ? 0 : (mk == all ? 2 : 1);
+  }
+}
+
+// Conv-tile prescan over x[B][H][W][T][Cin_p] fp16, one pass over the input.
+// CTA (b, band) streams R consecutive input rows of image b -- one contiguous
+// range of R * W * vpp 16-byte vectors -- and ORs every nonzero vector's
+// channel-chunk bit into the masks of the tiles whose receptive field holds
+// its pixel (input row / column -> tile-range tables), kept for the band's
+// tile rows in shared memory and flushed with atomicOr into the zeroed masks.
+// When 32 divides the vectors per pixel, a warp-wide load covers one pixel:
+// the lanes' bits are OR-reduced and the pixel's tiles updated once.
+constexpr int kMaxMapSide = 1024;  // H, W limits of the row / column tables
+constexpr int kMaxVpp = 1024;      // vector slots per pixel with a precomputed chunk bit
+constexpr int kMaxBandTiles = 2048;
+
 __global__ void __launch_bounds__(kPrescanThreads)
     prescan_conv_kernel(const __half* __restrict__ x, uint32_t* __restrict__ mask,
                         int64_t* nnz, int T, int B, int H, int W, int Cin_p, int KH, int KW,
-                        int s, int p, int Wb, int Hb, int Bb, int n_wt, int n_ht, int chunk) {
-  __shared__ uint32_t s_mask;
+                        int s, int p, int Wb, int Hb, int Bb, int n_wt, int n_ht, int chunk,
+                        int R, int lvpp) {
+  __shared__ uint32_t s_m[kMaxBandTiles];          // masks of the band's tile rows
+  __shared__ uint16_t s_row[2 * kMaxMapSide], s_col[2 * kMaxMapSide];  // (first tile, count)
+  __shared__ uint32_t s_cbit[kMaxVpp];
   __shared__ unsigned long long s_cnt;
-  const int mt = blockIdx.x;
-  const int wt = mt % n_wt;
-  const int ht = (mt / n_wt) % n_ht;
-  const int bt = mt / (n_wt * n_ht);
+  const int n_band = (H + R - 1) / R;
+  const int b = blockIdx.x / n_band;
+  const int band = blockIdx.x - b * n_band;
+  const int r0 = band * R, r1 = min(H, r0 + R);
   const int Ho = (H + 2 * p - KH) / s + 1;
   const int Wo = (W + 2 * p - KW) / s + 1;
-  const int oh0 = ht * Hb, oh1 = min(Ho, oh0 + Hb) - 1;
-  const int ow0 = wt * Wb, ow1 = min(Wo, ow0 + Wb) - 1;
-  // receptive field (rows/cols read by the conv for this tile)
-  const int rf_r0 = max(0, oh0 * s - p), rf_r1 = min(H, oh1 * s - p + KH);
-  const int rf_c0 = max(0, ow0 * s - p), rf_c1 = min(W, ow1 * s - p + KW);
-  // own region (each input element is counted by exactly one tile)
-  const int own_r0 = min(H, ht * Hb * s), own_r1 = (ht == n_ht - 1) ? H : min(H, (ht + 1) * Hb * s);
-  const int own_c0 = min(W, wt * Wb * s), own_c1 = (wt == n_wt - 1) ? W : min(W, (wt + 1) * Wb * s);
-  const bool count = nnz != nullptr;
-  const int r0 = count ? min(rf_r0, own_r0) : rf_r0;
-  const int r1 = count ? max(rf_r1, own_r1) : rf_r1;
-  const int c0 = count ? min(rf_c0, own_c0) : rf_c0;
-  const int c1 = count ? max(rf_c1, own_c1) : rf_c1;
-  const int b0 = bt * Bb, b1 = min(B, b0 + Bb);
-  if (threadIdx.x == 0) {
-    s_mask = 0;
-    s_cnt = 0;
+  const int vpp = T * Cin_p / 8;  // 16-byte vectors per pixel
+  // row / column tables: input index i feeds output indices o with
+  // o * s in [i + p - k + 1, i + p], o < n_out -> tiles o / tile
+  for (int i = threadIdx.x; i < H + W; i += blockDim.x) {
+    const bool is_row = i < H;
+    const int pos = is_row ? i : i - H;
+    const int n_out = is_row ? Ho : Wo, tb = is_row ? Hb : Wb, k = is_row ? KH : KW;
+    int olo = pos + p - k + 1, ohi = pos + p;
+    olo = olo <= 0 ? 0 : (olo + s - 1) / s;
+    ohi = ohi < 0 ? -1 : min(n_out - 1, ohi / s);
+    uint16_t first = 0, cntt = 0;
+    if (olo <= ohi) {
+      first = (uint16_t)(olo / tb);
+      cntt = (uint16_t)(ohi / tb - olo / tb + 1);
+    }
+    uint16_t* dst = is_row ? s_row + 2 * pos : s_col + 2 * pos;
+    dst[0] = first;
+    dst[1] = cntt;
   }
+  for (int v = threadIdx.x; v < vpp && v < kMaxVpp; v += blockDim.x)
+    s_cbit[v] = 1u << (((v * 8) % Cin_p) / chunk);
+  if (threadIdx.x == 0) s_cnt = 0;
   __syncthreads();
-  const int vec_per_pix = T * Cin_p / 8;  // 16-byte vectors per pixel
-  const int rh = max(0, r1 - r0), rw = max(0, c1 - c0), nb = max(0, b1 - b0);
-  const int npix = nb * rh * rw;
-  uint32_t m = 0;
+  // tile rows this band touches
+  int th_lo = 1 << 30, th_hi = -1;
+  for (int r = r0; r < r1; ++r) {
+    if (s_row[2 * r + 1]) {
+      th_lo = min(th_lo, (int)s_row[2 * r]);
+      th_hi = max(th_hi, (int)s_row[2 * r] + (int)s_row[2 * r + 1] - 1);
+    }
+  }
+  const int n_th = th_hi >= th_lo ? th_hi - th_lo + 1 : 0;
+  for (int i = threadIdx.x; i < n_th * n_wt; i += blockDim.x) s_m[i] = 0;
+  __syncthreads();
+  const bool count = nnz != nullptr;
   unsigned long long cnt = 0;
-  // Thread -> fixed vector slot v of a pixel (its channel chunk bit is then
-  // fixed too); pixels advance by a cursor (col, row, b), no divisions in the
-  // loop.  With more vectors per pixel than threads, each thread takes
-  // v = tid, tid + blockDim, ... of every pixel.
-  const int tid = threadIdx.x;
-  const bool rep = vec_per_pix <= (int)blockDim.x;
-  const int ppp = rep ? (int)blockDim.x / vec_per_pix : 1;  // pixels per pass
-  if (npix > 0 && (!rep || tid < ppp * vec_per_pix)) {
-    const int v0 = rep ? tid % vec_per_pix : tid;
-    int pix = rep ? tid / vec_per_pix : 0;
-    int col = pix % rw, row = (pix / rw) % rh, bb = pix / (rw * rh);
-    const int vstep = rep ? vec_per_pix : (int)blockDim.x;
-    constexpr int U = 4;  // pixels whose loads are in flight together
-    while (pix < npix) {
-      const uint4* px[U];
-      bool ok[U], in_rf[U], own[U];
+  const int row_vecs = W * vpp;
+  const int nvec = (r1 - r0) * row_vecs;  // < 2^31 (checked on the host)
+  const uint4* base = reinterpret_cast<const uint4*>(x) + ((int64_t)b * H + r0) * row_vecs;
+  const bool warp_uniform = (vpp % 32) == 0 && vpp <= kMaxVpp;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  // OR `bits` into the masks of every tile pixel (ih, col) feeds
+  auto scatter = [&](int ih, int col, uint32_t bits) {
+    const int tr0 = s_row[2 * ih], nr = s_row[2 * ih + 1];
+    const int tc0 = s_col[2 * col], nc = s_col[2 * col + 1];
+    for (int a = 0; a < nr; ++a)
+      for (int c = 0; c < nc; ++c) atomicOr(&s_m[(tr0 + a - th_lo) * n_wt + tc0 + c], bits);
+  };
+  if (warp_uniform) {
+    // a warp takes two pixels at a time: each lane loads vpp/32 vectors of
+    // each (eight loads in flight), ORs their chunk bits, the warp OR-reduces
+    // once per pixel and lane 0 updates the pixel's tiles
+    const int npix = (r1 - r0) * W, nj = vpp / 32;
+    for (int pa = 2 * warp; pa < npix; pa += 2 * nwarps) {
+      const int pb = pa + 1;
+      const bool hb = pb < npix;
+      const uint4* xa = base + (int64_t)pa * vpp + lane;
+      const uint4* xb = base + (int64_t)pb * vpp + lane;
+      uint32_t ba = 0, bb2 = 0;
+      for (int j0 = 0; j0 < nj; j0 += 4) {
+        uint4 q[8];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        ok[u] = pix < npix;
-        const int ih = r0 + row, iw = c0 + col;
-        px[u] = reinterpret_cast<const uint4*>(
-            x + (((int64_t)(b0 + bb) * H + ih) * W + iw) * (int64_t)T * Cin_p);
-        in_rf[u] = ih >= rf_r0 && ih < rf_r1 && iw >= rf_c0 && iw < rf_c1;
-        own[u] = count && ih >= own_r0 && ih < own_r1 && iw >= own_c0 && iw < own_c1;
-        // advance the cursor by ppp pixels
-        pix += ppp;
-        col += ppp;
-        while (col >= rw) {
-          col -= rw;
-          if (++row == rh) {
-            row = 0;
-            ++bb;
-          }
+        for (int u = 0; u < 4; ++u) {
+          const bool ok = j0 + u < nj;
+          q[u] = ok ? __ldg(xa + 32 * (j0 + u)) : make_uint4(0u, 0u, 0u, 0u);
+          q[4 + u] = (ok && hb) ? __ldg(xb + 32 * (j0 + u)) : make_uint4(0u, 0u, 0u, 0u);
         }
-      }
-      for (int v = v0; v < vec_per_pix; v += vstep) {
-        uint4 q[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) q[u] = ok[u] ? __ldg(px[u] + v) : make_uint4(0u, 0u, 0u, 0u);
-        const uint32_t cbit = 1u << (((v * 8) % Cin_p) / chunk);
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
+        for (int u = 0; u < 8; ++u) {
           const uint32_t w4[4] = {q[u].x & 0x7FFF7FFFu, q[u].y & 0x7FFF7FFFu,
                                   q[u].z & 0x7FFF7FFFu, q[u].w & 0x7FFF7FFFu};
           if ((w4[0] | w4[1] | w4[2] | w4[3]) == 0) continue;
-          if (in_rf[u]) m |= cbit;
-          if (own[u]) {
+          const uint32_t cb = s_cbit[lane + 32 * (j0 + (u & 3))];
+          if (u < 4) ba |= cb;
+          else bb2 |= cb;
+          if (count) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              cnt += ((w4[j] & 0xFFFFu) != 0) + ((w4[j] >> 16) != 0);
+            for (int k = 0; k < 4; ++k) cnt += ((w4[k] & 0xFFFFu) != 0) + ((w4[k] >> 16) != 0);
           }
         }
       }
+      ba = __reduce_or_sync(0xffffffffu, ba);
+      bb2 = __reduce_or_sync(0xffffffffu, bb2);
+      if (lane == 0) {
+        if (ba) {
+          const int rr = pa / W;
+          scatter(r0 + rr, pa - rr * W, ba);
+        }
+        if (hb && bb2) {
+          const int rr = pb / W;
+          scatter(r0 + rr, pb - rr * W, bb2);
+        }
+      }
+    }
+  } else {
+    const int step = blockDim.x;
+    for (int i0 = threadIdx.x; i0 < nvec; i0 += 8 * step) {
+      uint4 q[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * step;
+        q[u] = i < nvec ? __ldg(base + i) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * step;
+        const uint32_t w4[4] = {q[u].x & 0x7FFF7FFFu, q[u].y & 0x7FFF7FFFu,
+                                q[u].z & 0x7FFF7FFFu, q[u].w & 0x7FFF7FFFu};
+        if (i >= nvec || (w4[0] | w4[1] | w4[2] | w4[3]) == 0) continue;
+        if (count) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) cnt += ((w4[k] & 0xFFFFu) != 0) + ((w4[k] >> 16) != 0);
+        }
+        const int v = lvpp >= 0 ? (i & (vpp - 1)) : i % vpp;
+        const uint32_t bits = v < kMaxVpp ? s_cbit[v] : 1u << (((v * 8) % Cin_p) / chunk);
+        const int rr = i / row_vecs;
+        const int rem = i - rr * row_vecs;
+        const int col = lvpp >= 0 ? (rem >> lvpp) : rem / vpp;
+        scatter(r0 + rr, col, bits);
+      }
     }
   }
-  for (int off = 16; off; off >>= 1) {
-    m |= __shfl_xor_sync(0xffffffffu, m, off);
-    cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
-  }
-  if ((threadIdx.x & 31) == 0) {
-    if (m) atomicOr(&s_mask, m);
-    if (cnt) atomicAdd(&s_cnt, cnt);
+  if (count) {
+    for (int off = 16; off; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+    if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&s_cnt, cnt);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    mask[mt] = s_mask;
-    if (count && s_cnt) atomicAdd(reinterpret_cast<unsigned long long*>(nnz), s_cnt);
+  const int bt = b / Bb;
+  for (int i = threadIdx.x; i < n_th * n_wt; i += blockDim.x) {
+    const uint32_t mk = s_m[i];
+    if (!mk) continue;
+    const int th = th_lo + i / n_wt, tw = i - (i / n_wt) * n_wt;
+    atomicOr(mask + ((int64_t)bt * n_ht + th) * n_wt + tw, mk);
   }
+  if (threadIdx.x == 0 && count && s_cnt)
+    atomicAdd(reinterpret_cast<unsigned long long*>(nnz), s_cnt);
 }
 
 }  // namespace
@@ -270,19 +374,34 @@ int cf_prescan(const void* x, int x_fmt, int32_t* ag_mask, int32_t* tile_class, 
   const int64_t tiles = N * GH * GW;
   if (tiles == 0) return CF_OK;
   if (tiles > 0x7FFFFFFF) return fail(CF_ERR_UNSUPPORTED, "too many tiles");
+  if (GH * GW > kMaxTilesPerSample) return fail(CF_ERR_UNSUPPORTED, "too many tiles per sample");
+  if (H > 65535 || W > 65535) return fail(CF_ERR_UNSUPPORTED, "map too large");
   if (int rc = require_sm100()) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  prescan_ref_kernel<<<(unsigned)tiles, kPrescanThreads, 0, s>>>(
-      x, x_fmt, ag_mask, tile_class, (int)C, (int)H, (int)W, (int)H_out, (int)W_out, (int)k,
-      (int)stride, (int)pad, (int)BH, (int)BW, (int)GS, (int)G, (int)GH, (int)GW, threshold);
-  if (int rc = check_launch("prescan launch")) return rc;
-  if (nnz_out) {
-    const int64_t n = N * C * H * W;
-    int64_t blocks = (n + kPrescanThreads - 1) / kPrescanThreads;
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    count_nonzero_kernel<<<(unsigned)blocks, kPrescanThreads, 0, s>>>(x, x_fmt, n, nnz_out);
-    if (int rc = check_launch("count_nonzero launch")) return rc;
+  if (int rc = check_cuda(cudaMemsetAsync(ag_mask, 0, (size_t)tiles * sizeof(int32_t), s),
+                          "zero the masks"))
+    return rc;
+  const int n_cb = (int)((C + kRefChannelsPerCta - 1) / kRefChannelsPerCta);
+  const size_t smem = (size_t)GH * GW * 4 + (size_t)(H + W) * 4;
+  static std::atomic<bool> attr_done[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr_done[dev].load()) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(prescan_ref_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem),
+                            "cudaFuncSetAttribute(prescan)"))
+      return rc;
+    attr_done[dev].store(true);
   }
+  prescan_ref_kernel<<<(unsigned)(N * n_cb), kPrescanThreads, smem, s>>>(
+      x, x_fmt, ag_mask, nnz_out, (int)C, (int)H, (int)W, (int)H_out, (int)W_out, (int)k,
+      (int)stride, (int)pad, (int)BH, (int)BW, (int)GS, (int)GH, (int)GW, threshold);
+  if (int rc = check_launch("prescan launch")) return rc;
+  int64_t blocks = (tiles + 255) / 256;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  prescan_classify_kernel<<<(unsigned)blocks, 256, 0, s>>>(ag_mask, tile_class, tiles, (int)G);
+  if (int rc = check_launch("prescan classify launch")) return rc;
   return CF_OK;
 }
 
@@ -304,10 +423,31 @@ int cf_prescan_conv_tiles(const void* x, uint32_t* mask, int64_t* nnz_out, int64
   if (int rc = conv_geometry_for(T, B, Ho, Wo, Cout, Cin_p, stride, true, &TP, &Wb, &Hb, &Bb,
                                  &n_wt, &n_ht, &n_mt, &BK))
     return rc;
+  if (H > kMaxMapSide || W > kMaxMapSide) return fail(CF_ERR_UNSUPPORTED, "map too large for the prescan");
+  if ((int64_t)W * T * Cin_p / 8 > (1 << 24)) return fail(CF_ERR_UNSUPPORTED, "rows too long for the prescan");
+  const int64_t vpp = T * Cin_p / 8;
+  int lvpp = -1;  // log2 of the vectors per pixel when a power of two
+  for (int l = 0; l < 31; ++l)
+    if ((int64_t)1 << l == vpp) lvpp = l;
+  // rows per CTA: ~8K vectors each, but at least two CTAs per SM when possible
+  int64_t R = (8192 + W * vpp - 1) / (W * vpp);
+  if (R > H) R = H;
+  if (R < 1) R = 1;
+  while (R > 1 && B * ((H + R - 1) / R) < 2 * 148) R = (R + 1) / 2;
+  // the band's tile rows must fit the shared mask array
+  while (R > 1 && ((R * stride) / Hb + 3) * (int64_t)n_wt > kMaxBandTiles) R = (R + 1) / 2;
+  if ((R * stride / Hb + 3) * (int64_t)n_wt > kMaxBandTiles)
+    return fail(CF_ERR_UNSUPPORTED, "too many tile columns for the prescan");
   if (int rc = require_sm100()) return rc;
-  prescan_conv_kernel<<<n_mt, kPrescanThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  if (int rc = check_cuda(cudaMemsetAsync(mask, 0, (size_t)n_mt * sizeof(uint32_t),
+                                          static_cast<cudaStream_t>(stream)),
+                          "zero the tile masks"))
+    return rc;
+  const int64_t n_band = (H + R - 1) / R;
+  prescan_conv_kernel<<<(unsigned)(B * n_band), kPrescanThreads, 0,
+                        static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), mask, nnz_out, (int)T, (int)B, (int)H, (int)W, (int)Cin_p,
-      (int)KH, (int)KW, (int)stride, (int)pad, Wb, Hb, Bb, n_wt, n_ht, (int)chunk);
+      (int)KH, (int)KW, (int)stride, (int)pad, Wb, Hb, Bb, n_wt, n_ht, (int)chunk, (int)R, lvpp);
   return check_launch("prescan_conv launch");
 }
 

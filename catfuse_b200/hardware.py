@@ -1,19 +1,23 @@
 """HardwareProfile — per-GPU thresholds for the policy (reference:
 ``catfuse/hardware.py:23-179``), with a B200 profile registered for sm_100.
 
-The B200 numbers: HBM bandwidth and SM count come from the measured peaks
-file when present (``MEASURED_PEAKS.json`` at the repository root, written by
-the pool driver), else the nominal figures.  On B200 the fused tcgen05 kernel
-serves DenseKeep, SparseFlow and StaticZero alike, so the SparseFlow
-thresholds only decide where the prescan pass pays for itself: with few
-channels the dense tensor-core conv is already bandwidth-light.
+The B200 profile holds the nominal HBM figure and SM count.  On B200 the
+fused tcgen05 kernel serves DenseKeep, SparseFlow and StaticZero alike, so
+the SparseFlow thresholds only decide where the prescan pass pays for
+itself, and the runtime dispatch (EGD) is decided on the device from the
+prescan's tile masks: ``egd_max_active_frac`` is the largest fraction of
+active (tile, channel chunk) pairs for which the masked launch beats the
+dense one, calibrated on B200 with ``python -m catfuse_b200.hbm_bench``
+(config-2 sweep: masked time is linear in the active fraction; the value is
+the crossover with the dense launch, prescan included).  Profiles without a
+calibration keep the reference's element-sparsity rule (> 0.7 -> SparseFlow).
+``sparseflow_routing`` decides whether the shape policy sends memory-bound
+convs to SparseFlow at all (off on B200, see the profile's comment).
 """
 from __future__ import annotations
 
-import json
 import warnings
 from dataclasses import dataclass
-from pathlib import Path
 
 
 @dataclass(frozen=True)
@@ -28,6 +32,10 @@ class HardwareProfile:
     default_K_memory_bound: int
     default_K_compute_bound: int
     notes: str = ""
+    egd_max_active_frac: float = -1.0   # < 0: no device calibration (host rule)
+    # Static routing: whether memory-bound conv shapes go to SparseFlow
+    # (STFusionConvBNLIF, prescan + runtime EGD) at all.
+    sparseflow_routing: bool = True
 
     @property
     def sm_capability(self) -> int:
@@ -41,18 +49,10 @@ A100_40GB = HardwareProfile("A100 40GB", (8, 0), 1555.0, 40.0, 108, 128, 28, 8, 
 A100_80GB = HardwareProfile("A100 80GB", (8, 0), 2039.0, 40.0, 108, 128, 28, 8, 4)
 
 
-def _measured_hbm(default: float) -> float:
-    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
-    try:
-        return float(json.loads(p.read_text())["hbm_gbs"])
-    except Exception:
-        return default
-
-
 B200 = HardwareProfile(
     arch_name="B200",
     sm_version=(10, 0),
-    hbm_bandwidth_gbps=_measured_hbm(7700.0),
+    hbm_bandwidth_gbps=7700.0,
     l2_size_mb=126.0,
     sm_count=148,
     sf_threshold_C=256,
@@ -62,6 +62,14 @@ B200 = HardwareProfile(
     default_K_memory_bound=8,
     default_K_compute_bound=8,
     notes="sm_100a tcgen05 path; thresholds route the prescan, not the conv kernel",
+    egd_max_active_frac=0.5,
+    # Calibrated off: on B200 the prescan costs ~20 % of a dense 256-channel
+    # conv and the masked launch only wins below ~50 % active (tile, chunk)
+    # pairs; a 64-channel chunk of a 64-pixel x 4-step tile (plus halo) is
+    # empty only at per-element spike densities of ~1e-4, far below the 1-20 %
+    # of spiking ResNets, so every ResNet conv stays on DenseKeep.  SparseFlow
+    # (with the device EGD) remains available through force_sparse.
+    sparseflow_routing=False,
 )
 
 DEFAULT = B200

@@ -2,10 +2,11 @@
 
     python -m catfuse_b200.hbm_bench [--reps 10]
 
-Each call is timed alone with CUDA events, after a 256 MB write that evicts
-L2 (the write runs long enough for the host to queue the call behind it).
+Each call is captured into a CUDA graph and timed alone with CUDA events
+around its replay, after an L2 eviction (a 256 MB write, then a 256 MB read
+so that the flush leaves no dirty lines to write back inside the timed call).
 Achieved bandwidth = algorithmic bytes / time; the peak is ``hbm_gbs`` of
-MEASURED_PEAKS.json when present (copy bandwidth measured on this pool).
+MEASURED_PEAKS.json when present (a measured copy bandwidth of the GPU model).
 
 Cases (config numbers of BASELINE.json):
 * config 0 LIF family on z [T=4, B=32, 128, 32, 32]: lif_fwd (fp32 z -> fp16 /
@@ -24,7 +25,8 @@ from pathlib import Path
 
 import torch
 
-from . import ops
+from . import ops, workloads
+from .timing import L2Flush
 
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -37,36 +39,38 @@ def _peak():
 
 
 def _time(fn, reps, flush):
+    """Mean device time (us) of ``fn``'s launches: captured once into a CUDA
+    graph and replayed between two events, each replay after an L2-evicting
+    write, so host-side overhead of the Python wrappers is not timed."""
     fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        fn()
     torch.cuda.synchronize()
     ev = []
     for _ in range(reps):
-        flush.fill_(1.0)
+        flush()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        g.replay()
         b.record()
         ev.append((a, b))
     torch.cuda.synchronize()
     return sum(a.elapsed_time(b) for a, b in ev) / reps * 1e3  # us
 
 
-def _block_sparse(T, B, C, H, W, s, g, dev):
-    nb = (T, B, C // 32, (H + 7) // 8, (W + 7) // 8)
-    keep = (torch.rand(nb, generator=g) >= s).float()
-    keep = keep.repeat_interleave(32, 2).repeat_interleave(8, 3).repeat_interleave(8, 4)[..., :H, :W]
-    return (keep * (torch.rand(T, B, C, H, W, generator=g) < 0.3).float()).to(dev)
-
-
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--reps", type=int, default=20)
     args = ap.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
     peak, src = _peak()
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    flush = L2Flush(dev)
     g = torch.Generator().manual_seed(0)
     rows = []
 
@@ -97,14 +101,23 @@ def main(argv=None):
     sc = torch.ones(C, device=dev)
     sh = torch.zeros(C, device=dev)
     dense_us = None
-    for s in (0.8, 0.9, 0.95, 0.99, 1.0):
-        x = _block_sparse(T, B, C, H, W, s, g, dev)
+    sweep = []
+    geom = None
+    for s in (0.0, 0.8, 0.9, 0.95, 0.99, 1.0):
+        x = workloads.block_sparse_spikes(T, B, C, H, W, s, seed=int(s * 1000)).to(dev)
         xp = ops.pack_tbchw(x)
         wp = ops.pack_conv_weight(w, xp.shape[-1])
         xbytes = xp.numel() * 2
         mask = ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1)
-        us = _time(lambda: ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, mask_out=mask), args.reps, flush)
-        report(f"prescan_conv_tiles  x [32,28,28,4,256] fp16  s={s}", us, xbytes + 4 * mask.numel())
+        pre_us = _time(lambda: ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, mask_out=mask),
+                       args.reps, flush)
+        report(f"prescan_conv_tiles  x [32,28,28,4,256] fp16  s={s}", pre_us,
+               xbytes + 4 * mask.numel())
+        if geom is None:
+            geom = ops.conv_geometry(T, B, H, W, C, xp.shape[-1], 1, True)
+        n_kx = xp.shape[-1] // ops.conv_chunk(xp.shape[-1], True)
+        active = int(sum(bin(int(m) & ((1 << n_kx) - 1)).count("1") for m in mask.cpu().tolist()))
+        frac = active / (geom["n_mtiles"] * n_kx)
         v = torch.empty(B, H, W, C, device=dev)
         out = torch.empty(B, H, W, T, C, dtype=torch.float16, device=dev)
         conv_bytes = xbytes + wp.numel() * 2 + out.numel() * 2 + v.numel() * 4
@@ -116,7 +129,46 @@ def main(argv=None):
                   f"{dense_us:8.1f} us  {flops / dense_us / 1e6:7.0f} TFLOP/s dense-equivalent")
         us = _time(lambda: ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, v_out=v, out=out, tile_mask=mask),
                    args.reps, flush)
-        report(f"sparse conv_bn_lif (masked) s={s}  [{us / dense_us:.2f}x dense time]", us, conv_bytes)
+        report(f"sparse conv_bn_lif (masked, chunk 32) s={s} active={frac:.3f} "
+               f"[{us / dense_us:.2f}x dense, +prescan {(us + pre_us) / dense_us:.2f}x]",
+               us, conv_bytes)
+        # device EGD: dense-chunk masks, the kernel decides
+        emask = ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, egd=True)
+        n_kd = xp.shape[-1] // ops.conv_chunk(xp.shape[-1], False)
+        efrac = sum(bin(int(m) & ((1 << n_kd) - 1)).count("1") for m in emask.cpu().tolist()) / (
+            geom["n_mtiles"] * n_kd)
+        emasked = _time(lambda: ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, v_out=v, out=out,
+                                                tile_mask=emask, egd_max_active_frac=1.0),
+                        args.reps, flush)
+        from .hardware import B200
+        theta = B200.egd_max_active_frac
+
+        def egd_total():
+            ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, mask_out=emask, egd=True)
+            ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, v_out=v, out=out, tile_mask=emask,
+                            egd_max_active_frac=theta)
+        etot = _time(egd_total, args.reps, flush)
+        print(f"{'  device EGD (prescan + conv, max_active ' + str(theta) + ')':58s} {etot:8.1f} us"
+              f"  [{etot / dense_us:.2f}x dense]  active(chunk 64)={efrac:.3f}, "
+              f"masks forced {emasked:.1f} us")
+        sweep.append({"s": s, "active_frac": efrac, "masked_us": emasked, "prescan_us": pre_us,
+                      "dense_us": dense_us, "egd_total_us": etot,
+                      "active_frac_chunk32": frac, "masked_chunk32_us": us})
+    # EGD calibration: masked time ~ a + b * active_frac (least squares over the
+    # sweep); SparseFlow pays off while prescan + masked < dense, i.e. below
+    # the crossover fraction written out here.
+    xs = [r["active_frac"] for r in sweep]
+    ys = [r["masked_us"] for r in sweep]
+    n = len(xs)
+    mx, my = sum(xs) / n, sum(ys) / n
+    sxx = sum((a - mx) ** 2 for a in xs)
+    b = sum((a - mx) * (c - my) for a, c in zip(xs, ys)) / sxx if sxx > 0 else 0.0
+    a0 = my - b * mx
+    pre = sum(r["prescan_us"] for r in sweep) / n
+    cross = (dense_us - pre - a0) / b if b > 0 else 0.0
+    print(json.dumps({"egd_calibration": {"masked_us_fit": [a0, b], "prescan_us": pre,
+                                          "dense_us": dense_us,
+                                          "crossover_active_frac": cross, "sweep": sweep}}))
     xr = x.reshape(T * B, C, H, W).half().contiguous()
     us = _time(lambda: ops.prescan(xr, 3, 1, 1, 8, 8, 32), args.reps, flush)
     report("prescan (reference geometry) x [128,256,28,28] fp16", us, xr.numel() * 2)

@@ -69,7 +69,10 @@ def check_input(x: torch.Tensor, spec: ConvLIFSpec):
 
 def fused_forward(x: torch.Tensor, spec: ConvLIFSpec, params: ConvLIFParams, state,
                   cache: _WeightCache, sparse: bool, out_dtype=torch.float32,
-                  stats: Optional[dict] = None, precision: str = "fp16") -> torch.Tensor:
+                  stats: Optional[dict] = None, precision: str = "fp16",
+                  egd_max_active_frac: Optional[float] = None) -> torch.Tensor:
+    """``sparse``: prescan + masked conv; with ``egd_max_active_frac`` the
+    kernel decides on the device whether the masks run (EGD)."""
     check_input(x, spec)
     T, B, Cin, H, W = x.shape
     Ho, Wo = spec.output_hw(H, W)
@@ -83,12 +86,14 @@ def fused_forward(x: torch.Tensor, spec: ConvLIFSpec, params: ConvLIFParams, sta
     if sparse:
         nnz = torch.zeros(1, dtype=torch.int64, device=dev) if stats is not None else None
         mask = ops.prescan_conv_tiles(xp, Cout, spec.kernel_size, spec.kernel_size, spec.stride,
-                                      spec.padding, nnz_out=nnz)
+                                      spec.padding, nnz_out=nnz,
+                                      egd=egd_max_active_frac is not None)
         if stats is not None:
             stats["nnz"] = nnz
             stats["tile_mask"] = mask
     out = ops.conv_bn_lif(xp, wp, scale, shift, spec.stride, spec.padding, v_in=v_in,
-                          v_out=v_out, tile_mask=mask, lif=spec.lif_config(), precision=precision)
+                          v_out=v_out, tile_mask=mask, lif=spec.lif_config(), precision=precision,
+                          egd_max_active_frac=egd_max_active_frac if sparse else None)
     state.set_native(v_out)
     return ops.unpack_bhwtc(out, dtype=out_dtype)
 

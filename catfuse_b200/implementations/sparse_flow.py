@@ -28,8 +28,9 @@ class SparseFlow(Implementation):
     def reset_caches(self) -> None:
         self._cache.reset()
 
-    def forward(self, x, spec, params, state, stats=None):
-        return fused_forward(x, spec, params, state, self._cache, sparse=True, stats=stats)
+    def forward(self, x, spec, params, state, stats=None, egd_max_active_frac=None):
+        return fused_forward(x, spec, params, state, self._cache, sparse=True, stats=stats,
+                             egd_max_active_frac=egd_max_active_frac)
 
     def forward_with_k(self, x, spec, params, state, K=None):
         """TimeBlock(K): chunks of K steps, v carried through the StateBuffer;

@@ -166,7 +166,7 @@ class NetworkPlan:
             elif precision == "fp32" and ops.planes_ok(spec.out_channels, c_):
                 prec, sparse = "planes", False   # the plane mode runs dense
             else:
-                prec = "split"
+                prec, sparse = "split", False    # device EGD runs fp16 weights
             self.steps.append(ConvStep(name, nat, src, dst, identity, res_mode,
                                        _lif_of(pat) if lif else None, sparse, prec=prec))
             return dst
@@ -237,6 +237,9 @@ class NetworkPlan:
                     cin_p = self.shapes[st.src][-1]
                     g = ops.conv_geometry(t_, b_, ho, wo, co, cin_p, st.stride, True)
                     st.mask = torch.zeros(g["n_mtiles"], dtype=torch.int32, device=self.device)
+        from .hardware import detect_hardware
+        frac = detect_hardware().egd_max_active_frac
+        self.egd_frac = frac if frac >= 0 else 1.0
         self.fresh = True
         self._graphs = {}
 
@@ -266,7 +269,7 @@ class NetworkPlan:
             if st.sparse:
                 ops.prescan_conv_tiles(self.acts[st.src], spec.out_channels, spec.kernel_size,
                                        spec.kernel_size, spec.stride, spec.padding,
-                                       mask_out=st.mask)
+                                       mask_out=st.mask, egd=True)
             ident = self.acts[st.identity] if st.identity is not None else None
             if st.lif is None:
                 ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
@@ -278,7 +281,8 @@ class NetworkPlan:
                                 res_mode=st.res_mode if ident is not None else "none",
                                 v_in=None if fresh else st.v, v_out=st.v,
                                 tile_mask=st.mask if st.sparse else None, lif=st.lif,
-                                out=self.acts[st.dst], precision=st.prec)
+                                out=self.acts[st.dst], precision=st.prec,
+                                egd_max_active_frac=self.egd_frac if st.sparse else None)
         ops.avgpool_fc(self.acts[self.final], self.fc_w, self.fc_b, out=self.logits)
 
     def run(self, use_graph: bool = True):
@@ -321,7 +325,7 @@ class CTFNetwork(nn.Module):
     """Wraps a rewritten spiking ResNet; ``forward(x[T, B, C, H, W])`` runs the
     native plan and returns logits [T, B, classes] (fp32)."""
 
-    def __init__(self, model: nn.Module, use_graph: bool = True, use_sparse: bool = False,
+    def __init__(self, model: nn.Module, use_graph: bool = True, use_sparse: bool = True,
                  precision: str = "fp16"):
         super().__init__()
         if precision not in NETWORK_PRECISIONS:

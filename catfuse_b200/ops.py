@@ -395,12 +395,16 @@ def conv_bn_lif(x: torch.Tensor, wp: torch.Tensor, scale: Optional[torch.Tensor]
                 identity: Optional[torch.Tensor] = None, res_mode=None,
                 v_in: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None,
                 tile_mask: Optional[torch.Tensor] = None, lif: LIFConfig = _DEFAULT_LIF,
-                out: Optional[torch.Tensor] = None, precision: str = "fp16"):
+                out: Optional[torch.Tensor] = None, precision: str = "fp16",
+                egd_max_active_frac: Optional[float] = None):
     """Fused conv+BN+LIF on x[B,H,W,T,Cin_p] fp16 with wp[Cout,KH,KW,Cin_p] fp16
     (precision "fp16"), split weights wp[Cout,KH,KW,2*Cin_p] from
     pack_conv_weight_split (precision "split") or digit planes
     wp[Cout,KH,KW,3*Cin_p] from pack_conv_weight_planes (precision "planes");
     for the last two the scale is already divided by the prescale.
+    ``egd_max_active_frac`` (with ``tile_mask``): decide on the device whether
+    the masks run (at most that fraction of (tile, chunk) pairs active) or
+    the launch runs dense; the result is identical either way.
 
     Returns out[B,Ho,Wo,T,Cout] fp16.  v_out (if given) receives v_T in
     [B,Ho,Wo,Cout] fp32; v_in may alias v_out."""
@@ -440,6 +444,14 @@ def conv_bn_lif(x: torch.Tensor, wp: torch.Tensor, scale: Optional[torch.Tensor]
         _lib.call("cf_conv_bn_lif_planes", x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
                   _ptr(identity), mode, _ptr(v_in), _ptr(v_out), out.data_ptr(),
                   T, B, H, W, Cin_p, Cout, KH, KW, stride, pad, *lif.args(), _stream())
+        return out
+    if egd_max_active_frac is not None:
+        if tile_mask is None or precision != "fp16":
+            raise ValueError("the device dispatch needs a tile mask and fp16 weights")
+        _lib.call("cf_conv_bn_lif_egd", x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
+                  _ptr(identity), mode, _ptr(v_in), _ptr(v_out), out.data_ptr(),
+                  _ptr(tile_mask), T, B, H, W, Cin_p, Cout, KH, KW, stride, pad, *lif.args(),
+                  float(egd_max_active_frac), _stream())
         return out
     fn = "cf_conv_bn_lif_split" if precision == "split" else "cf_conv_bn_lif"
     _lib.call(fn, x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
@@ -508,14 +520,16 @@ def prescan(x: torch.Tensor, k: int, stride: int, pad: int, BH: int, BW: int, GS
 
 def prescan_conv_tiles(x: torch.Tensor, Cout: int, KH: int, KW: int, stride: int, pad: int,
                        mask_out: Optional[torch.Tensor] = None,
-                       nnz_out: Optional[torch.Tensor] = None):
-    """Conv-tile prescan over x[B,H,W,T,Cin_p] fp16 -> per-M-tile chunk mask."""
+                       nnz_out: Optional[torch.Tensor] = None, egd: bool = False):
+    """Conv-tile prescan over x[B,H,W,T,Cin_p] fp16 -> per-M-tile chunk mask
+    (the chunk of masked launches, or with ``egd`` the dense chunk that the
+    device-dispatch launches use)."""
     _need(x, "x", torch.float16)
     B, H, W, T, Cin_p = x.shape
     Ho = (H + 2 * pad - KH) // stride + 1
     Wo = (W + 2 * pad - KW) // stride + 1
     g = conv_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, True)
-    chunk = conv_chunk(Cin_p, True)
+    chunk = conv_chunk(Cin_p, not egd)
     if mask_out is None:
         mask_out = torch.empty(g["n_mtiles"], dtype=torch.int32, device=x.device)
     if nnz_out is not None:

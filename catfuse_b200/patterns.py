@@ -20,6 +20,8 @@ Every pattern also exposes ``native_conv()`` (where it is a convolution) so
 """
 from __future__ import annotations
 
+import math
+
 from typing import Optional
 
 import torch
@@ -371,9 +373,37 @@ class STFusionConvBNLIF(CTFPattern, _ConvPatternMixin):
                 self.last_dispatch = "DenseKeep"
                 out = self._dense_forward(x)
         else:
-            self.last_dispatch = "SparseFlow(device)"
-            out = self._batchfold_forward(x)
+            # device-side EGD: the prescan's tile masks feed the kernel, which
+            # counts the active (tile, chunk) pairs and runs the masks or the
+            # dense schedule (calibrated threshold of the hardware profile);
+            # no host synchronisation.  dispatch_decision() reads it back.
+            from .hardware import detect_hardware
+            frac = detect_hardware().egd_max_active_frac
+            self._egd_stats = {}
+            out = self._impl_sparse.forward(x, self.spec, self._ensure_params(), self.state,
+                                            stats=self._egd_stats,
+                                            egd_max_active_frac=frac if frac >= 0 else 1.0)
+            self._egd_frac = frac if frac >= 0 else 1.0
+            self.last_dispatch = "EGD(device)"
         return out.squeeze(0) if squeeze else out
+
+    def dispatch_decision(self) -> Optional[str]:
+        """What the device-side EGD of the last forward chose: "StaticZero"
+        (no active chunk), "SparseFlow" (masks ran) or "DenseKeep" (reads the
+        tile masks back: synchronises)."""
+        st = getattr(self, "_egd_stats", None)
+        if not st or "tile_mask" not in st:
+            return self.last_dispatch
+        from . import ops
+        mask = st["tile_mask"]
+        cin_p = ops.pad16(self.in_channels)
+        n_kx = cin_p // ops.conv_chunk(cin_p, False)   # device-dispatch masks: dense chunk
+        bits = (1 << n_kx) - 1
+        active = sum(bin(int(m) & bits).count("1") for m in mask.cpu().tolist())
+        if active == 0:
+            return "StaticZero"
+        limit = math.floor(self._egd_frac * mask.numel() * n_kx)
+        return "SparseFlow" if active <= limit else "DenseKeep"
 
     def extra_repr(self):
         s = f"{self.in_channels}, {self.out_channels}, kernel_size={self.kernel_size}, K={self.K}"

@@ -108,6 +108,10 @@ def get_policy(pattern: str, C_in: int = 0, C_out: int = 0, H: int = 0, W: int =
     else:
         regime = classify_shape_regime(C_in, C_out, H, W, kernel_size, hwprof)
     row = _DEFAULT_TABLE.get((pattern, regime))
+    if (row is not None and row.spatial_backend == SpatialBackend.SPARSE_FLOW
+            and not getattr(_hw(hwprof), "sparseflow_routing", True)):
+        row = PolicyRow(row.pattern, row.shape_regime, row.K, SpatialBackend.DENSE_KEEP,
+                        row.fusion_mode, row.io_ratio)
     if row is not None:
         if row.K == 0:
             return PolicyRow(row.pattern, row.shape_regime, T, row.spatial_backend, row.fusion_mode,

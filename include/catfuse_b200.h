@@ -247,6 +247,28 @@ CF_API int cf_maxpool_bhwtc(const void* x, void* y, int64_t B, int64_t H, int64_
                             int64_t T, int64_t C, int64_t k, int64_t stride, int64_t pad,
                             void* stream);
 
+/* cf_conv_bn_lif with SparseFlow / DenseKeep chosen on the device: the
+ * kernel counts the active (tile, chunk) pairs of `tile_mask`
+ * (cf_prescan_conv_tiles) before its pipeline starts and runs the masks only
+ * if at most max_active_frac of all pairs are active, otherwise every chunk of
+ * every tile (an all-zero input leaves every mask empty: StaticZero).  The
+ * masks use the dense channel chunk: cf_prescan_conv_tiles with
+ * chunk = cf_conv_chunk(Cin_p, 0).  No host
+ * synchronisation, so it can sit inside a CUDA graph.  The result is the same
+ * bit for bit either way; only the speed differs.  Replaces the runtime EGD of
+ * STFusionConvBNLIF.forward (catfuse/sparseflow/ops/st_fusion_conv_bn_lif.py:
+ * 510-524: sparsity = 1 - nnz/numel read on the host, > 0.7 -> SparseFlow),
+ * with the measured work (active pairs) in place of the element count. */
+CF_API int cf_conv_bn_lif_egd(const void* x, const void* wp, const float* scale,
+                              const float* shift, const void* identity, int res_mode,
+                              const float* v_in, float* v_out, void* out,
+                              const uint32_t* tile_mask,
+                              int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin_p,
+                              int64_t Cout, int64_t KH, int64_t KW, int64_t stride,
+                              int64_t pad, float tau, float v_threshold, float v_reset,
+                              int hard_reset, int decay_input, float max_active_frac,
+                              void* stream);
+
 /* Extended-precision variant of cf_conv_bn_lif: the weight is carried as two
  * fp16 parts, wp2[Cout][KH][KW][2][Cin_p] = {hi, lo} (cf_pack_conv_weight_split),
  * and every (tap, channel chunk) issues the hi and the lo MMAs into the same

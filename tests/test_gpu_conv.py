@@ -421,3 +421,27 @@ def test_conv_planes_vs_fp32_oracle(dev, shape, mode):
     _, _, h32 = lif_trace(z32)
     check_lif_parity(got, vg, ref, v32, h32, v_tol=1e-4, near_tol=1e-5, max_flip_rate=1e-4,
                      what=f"planes {mode} {shape}")
+
+
+@pytest.mark.parametrize("sparsity", [0.0, 0.9, 0.99, 1.0])
+def test_device_egd_dispatch_bit_identical(dev, sparsity):
+    """Device-side EGD: whatever the kernel decides (masks or dense), the
+    result equals the plain masked launch and the dense launch of the same
+    geometry bit for bit, at thresholds that force either choice."""
+    ops = _ops()
+    T, B, C, H, W = 4, 8, 256, 28, 28
+    x = workloads.block_sparse_spikes(T, B, C, H, W, sparsity, seed=51)
+    _, w, scale, shift = _case(1, 1, C, C, 1, 1, 3, seed=52)
+    xp = ops.pack_tbchw(x.to(dev))
+    wp = ops.pack_conv_weight(w.to(dev), xp.shape[-1])
+    sc, sh = scale.to(dev), shift.to(dev)
+    mask = ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, egd=True)   # dense-chunk masks
+    ref = ops.conv_bn_lif(xp, wp, sc, sh, 1, 1)                  # dense launch, same chunk
+    for frac in (0.0, 0.3, 1.0):
+        got = ops.conv_bn_lif(xp, wp, sc, sh, 1, 1, tile_mask=mask, egd_max_active_frac=frac)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), frac
+    # the masks of the dense chunk match the oracle
+    geom = ops.conv_geometry(T, B, H, W, C, xp.shape[-1], 1, True)
+    m_o = _conv_tile_mask_oracle(xp.cpu().numpy(), geom, 3, 3, 1, 1, ops.conv_chunk(xp.shape[-1], False))
+    assert np.array_equal(mask.cpu().numpy().astype(np.int64) & 0xFFFFFFFF, m_o)

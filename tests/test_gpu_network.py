@@ -401,3 +401,31 @@ def test_avgpool_fc_head(dev):
     out0 = ops.avgpool_fc(xp, fc_w.to(dev), None).cpu()
     ref0 = torch.nn.functional.linear(x.double().mean(dim=(3, 4)), fc_w.double())
     assert (out0.double() - ref0).abs().max() <= 1e-5
+
+
+def test_network_device_egd_equals_dense(dev):
+    """SEW-ResNet-18 with every 3x3/s1 conv forced onto STFusion: the native
+    plan's prescan + device-side EGD gives the same logits bit for bit as the
+    dense plan, on inputs whose left half is zero (so some tiles are empty and
+    the kernel's choice differs per layer)."""
+    from catfuse_b200.network import CTFNetwork
+    from catfuse_b200.substitute import substitute_sf
+    from catfuse_b200 import hardware
+    from catfuse_b200.sj import functional
+    net, x = _sew_net(B=8, seed=4)
+    x = x.clone()
+    x[..., :16] = 0.0
+    m, st = substitute_sf(net, T=4, force_sparse=True, hwprof=hardware.B200)
+    assert st["patterns_matched"].get("STFusionConvBNLIF", 0) > 6
+    m = m.to(dev)
+    sparse = CTFNetwork(m, use_sparse=True)
+    dense = CTFNetwork(m, use_sparse=False)
+    xd = x.to(dev)
+    functional.reset_net(sparse)
+    functional.reset_net(dense)
+    a = sparse(xd)
+    b = dense(xd)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    plan = sparse.plan_for(xd)
+    assert sum(1 for s in plan.steps if getattr(s, "sparse", False)) > 6

@@ -22,8 +22,13 @@ def test_policy_table_and_formulas():
     assert policy.classify_shape_regime(64, 64, 32, 32, 3, v100) == "compute_bound"
     assert policy.classify_shape_regime(512, 512, 56, 56, 3, v100) == "compute_bound"
     assert policy.classify_shape_regime(64, 64, 32, 32, 1, v100) == "memory_bound"
-    r = policy.get_policy("Conv3x3_BN_LIF", 256, 256, 8, 8, 3, T=4)
+    r = policy.get_policy("Conv3x3_BN_LIF", 256, 256, 8, 8, 3, T=4, hwprof=v100)
     assert r.spatial_backend == policy.SpatialBackend.SPARSE_FLOW and r.K == 8
+    # B200 calibration: the shape stays memory-bound but routes to DenseKeep
+    b200 = hardware.B200
+    r = policy.get_policy("Conv3x3_BN_LIF", 256, 256, 8, 8, 3, T=4, hwprof=b200)
+    assert r.spatial_backend == policy.SpatialBackend.DENSE_KEEP and r.K == 8
+    assert 0.0 < b200.egd_max_active_frac < 1.0
     r = policy.get_policy("Linear_LIF", T=6)
     assert r.K == 6 and r.spatial_backend == policy.SpatialBackend.DENSE_KEEP
     r = policy.get_policy("Unknown_Pattern", 64, 64, 8, 8, 3, T=2)
@@ -86,11 +91,19 @@ def test_substitute_sew_resnet18_routing():
     from catfuse_b200.substitute import substitute, substitute_sf
     from catfuse_b200.patterns import PartialFusionConvBNLIF, STFusionConvBNLIF, CTFSEWBasicBlock
     net = zoo.init_random_(zoo.build_sew_resnet18_cifar())
-    m, st = substitute_sf(net, T=4)
+    # the reference's thresholds (V100 profile): 6 memory-bound sites -> SparseFlow
+    m, st = substitute_sf(net, T=4, hwprof=hardware.V100_PCIE_32GB)
     assert st["total_lif_nodes"] == 20 and st["fused_lif_nodes"] == 20
     assert st["coverage_pct"] == 100.0
     assert isinstance(m.conv1, PartialFusionConvBNLIF) and isinstance(m.bn1, nn.Identity)
     assert isinstance(m.layer4[1].conv2, STFusionConvBNLIF)
+    assert st["patterns_matched"]["STFusionConvBNLIF"] == 6
+    # the calibrated B200 profile keeps every site on DenseKeep ...
+    mb, stb = substitute_sf(net, T=4, hwprof=hardware.B200)
+    assert "STFusionConvBNLIF" not in stb["patterns_matched"]
+    # ... unless SparseFlow is forced (then the native plan runs the device EGD)
+    mf, stf = substitute_sf(net, T=4, force_sparse=True, hwprof=hardware.B200)
+    assert stf["patterns_matched"]["STFusionConvBNLIF"] > 6
     assert isinstance(m.layer2[0].downsample[0], PartialFusionConvBNLIF)
     names = [r["name"] for r in st["routing"]]
     assert len(names) == len(set(names)) == 20
