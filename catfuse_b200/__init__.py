@@ -36,6 +36,11 @@ def optimize(model, device="cuda:0", policy=None, T=16, use_sparseflow=True, nat
         new_model = new_model.to(device)
     stats["native_plan"] = False
     if native:
+        from .spikformer_net import CTFSpikformer, is_spikformer
+        if is_spikformer(new_model):
+            net = CTFSpikformer(new_model, use_graph=use_graph, precision=precision)
+            stats["native_plan"] = True
+            return net, stats
         from .network import CTFNetwork, UnsupportedTopology
         try:
             # STFusion sites keep their runtime dispatch inside the native plan:

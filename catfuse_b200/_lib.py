@@ -74,6 +74,8 @@ SIGNATURES = {
                                      _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _INT,
                                      _INT, _P]),
     "cf_pack_conv_weight_planes": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
+    "cf_token_mean_lif_fc": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F,
+                                    _F, _INT, _INT, _P]),
     "cf_set_wait_limit": (_INT, [ctypes.c_uint32]),
     "cf_test_arm_stalled_load": (_INT, [_INT]),
     "cf_avgpool_fc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),

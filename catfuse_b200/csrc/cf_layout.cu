@@ -192,6 +192,39 @@ __global__ void avgpool_fc_kernel(const __half* __restrict__ x, const float* __r
   }
 }
 
+// Spikformer head: per sample b, the token mean m_t[c] = sum_n x[b][n][t][c] / N
+// (x holds integer spike counts: the fp32 sum is exact), the pre-head LIF over
+// t (one thread per channel, membrane in a register), the spikes kept in
+// shared memory, then logits[t][b][k] = sum_c s_t[c] * fc_w[k][c] + fc_b[k]
+// with one warp per (t, k).
+__global__ void token_mean_lif_fc_kernel(const __half* __restrict__ x, const float* __restrict__ v_in,
+                                         float* __restrict__ v_out, const float* __restrict__ fc_w,
+                                         const float* __restrict__ fc_b, float* __restrict__ logits,
+                                         int T, int B, int N, int C, int K, LifParams lp) {
+  extern __shared__ float s_spk[];  // [T][C]
+  const int b = blockIdx.x;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float v = v_in ? v_in[(int64_t)b * C + c] : 0.f;
+    for (int t = 0; t < T; ++t) {
+      const __half* p = x + (((int64_t)b * N) * T + t) * C + c;
+      float sum = 0.f;
+      for (int n = 0; n < N; ++n) sum = __fadd_rn(sum, __half2float(p[(int64_t)n * T * C]));
+      const float m = __fdiv_rn(sum, (float)N);
+      s_spk[t * C + c] = lif_step(v, m, lp);
+    }
+    if (v_out) v_out[(int64_t)b * C + c] = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int tk = warp; tk < T * K; tk += nw) {
+    const int t = tk / K, k = tk - t * K;
+    float acc = 0.f;
+    for (int c = lane; c < C; c += 32) acc = fmaf(s_spk[t * C + c], fc_w[(int64_t)k * C + c], acc);
+    for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) logits[((int64_t)t * B + b) * K + k] = acc + (fc_b ? fc_b[k] : 0.f);
+  }
+}
+
 // Max pool over x[B][H][W][T][C] fp16 (padding = -inf), one thread per
 // output element group of 8 channels (16-byte vectors).
 __global__ void maxpool_kernel(const __half* __restrict__ x, __half* __restrict__ y, int B, int H,
@@ -378,6 +411,22 @@ static int im2col_impl(const void* x, int x_fmt, void* y, int64_t T, int64_t B, 
       x, x_fmt, static_cast<__half*>(y), (int)T, (int)B, (int)C, (int)H, (int)W, (int)Ho,
       (int)Wo, (int)k, (int)stride, (int)pad, (int)Kp, split);
   return check_launch("im2col launch");
+}
+
+int cf_token_mean_lif_fc(const void* x, const float* v_in, float* v_out, const float* fc_w,
+                         const float* fc_b, float* logits, int64_t T, int64_t B, int64_t N,
+                         int64_t C, int64_t K, float tau, float v_threshold, float v_reset,
+                         int hard_reset, int decay_input, void* stream) {
+  if (!x || !fc_w || !logits) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
+  if (T <= 0 || B <= 0 || N <= 0 || C <= 0 || K <= 0) return fail(CF_ERR_INVALID_ARG, "bad shape");
+  if (!(tau > 0.f)) return fail(CF_ERR_INVALID_ARG, "tau must be > 0");
+  if (T * C * 4 > 48 * 1024) return fail(CF_ERR_UNSUPPORTED, "T * C too large for the head kernel");
+  if (int rc = require_sm100()) return rc;
+  token_mean_lif_fc_kernel<<<(unsigned)B, 256, (size_t)(T * C) * 4,
+                             static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), v_in, v_out, fc_w, fc_b, logits, (int)T, (int)B, (int)N,
+      (int)C, (int)K, make_lif(tau, v_threshold, v_reset, hard_reset, decay_input));
+  return check_launch("token_mean_lif_fc launch");
 }
 
 int cf_pack_im2col(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64_t C, int64_t H,

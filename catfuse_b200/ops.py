@@ -22,7 +22,7 @@ __all__ = [
     "conv_geometry", "prescan", "prescan_conv_tiles", "conv_chunk", "avgpool_fc", "maxpool_bhwtc",
     "pad16", "SPIKE_FORMATS", "RES_MODES", "PRECISIONS", "pack_conv_weight_split",
     "pack_im2col_split", "im2col_weight_split", "split_prescale", "check_device_error",
-    "set_wait_limit",
+    "set_wait_limit", "token_mean_lif_fc",
 ]
 
 # Operand precision of the fused conv: "fp16" = fp16 weights (spikes are exact
@@ -586,3 +586,19 @@ def set_wait_limit(max_polls: int = 0) -> None:
     """Bound on the polls of every device-side wait of later conv launches
     (0 restores the default of 2^24 polls)."""
     _lib.call("cf_set_wait_limit", int(max_polls))
+
+
+def token_mean_lif_fc(x: torch.Tensor, fc_w: torch.Tensor, fc_b: Optional[torch.Tensor],
+                      v_in: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None,
+                      lif: LIFConfig = _DEFAULT_LIF, out: Optional[torch.Tensor] = None):
+    """Spikformer head over tokens x[B,N,T,C] fp16: token mean -> LIF -> fc.
+    -> logits[T,B,K] fp32; v_in / v_out [B,C] fp32 carry the LIF state."""
+    _need(x, "x", torch.float16)
+    _need(fc_w, "fc_w", torch.float32)
+    B, N, T, C = x.shape
+    K = fc_w.shape[0]
+    if out is None:
+        out = torch.empty((T, B, K), dtype=torch.float32, device=x.device)
+    _lib.call("cf_token_mean_lif_fc", x.data_ptr(), _ptr(v_in), _ptr(v_out), fc_w.data_ptr(),
+              _ptr(fc_b), out.data_ptr(), T, B, N, C, K, *lif.args(), _stream())
+    return out

@@ -352,6 +352,18 @@ CF_API int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b,
                   float* logits, int64_t T, int64_t B, int64_t H, int64_t W,
                   int64_t C, int64_t K, void* stream);
 
+/* Spikformer head: token mean over x[B][N][T][C] fp16 (spike counts), the
+ * pre-head LIF over t (v_in / v_out [B][C] fp32, either may be NULL), then
+ * logits[T][B][K] = s_t @ fc_w[K][C]^T + fc_b (fc_b may be NULL).  Replaces
+ * forward_features' y.mean(dim=2) -> pre_head_lif -> head
+ * (models/spikformer_github.py:311-329), the avgpool_lif pattern of the
+ * reference (catfuse/kernels/avgpool_lif.py:61-145) over the token axis. */
+CF_API int cf_token_mean_lif_fc(const void* x, const float* v_in, float* v_out,
+                                const float* fc_w, const float* fc_b, float* logits,
+                                int64_t T, int64_t B, int64_t N, int64_t C, int64_t K,
+                                float tau, float v_threshold, float v_reset, int hard_reset,
+                                int decay_input, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
