@@ -257,6 +257,66 @@ def egd_report(plan):
     return {"max_active_frac": plan.egd_frac, "sites": out} if out else None
 
 
+def other_workloads(dev, flush, steps, dist, world):
+    """The other BASELINE configurations, same protocol (graph replay, inputs
+    resident, L2 flushed between steps, CUDA events, max over ranks):
+    config 3 Spiking ResNet-18 224x224 B=32 (dense plan, and every 3x3/s1 conv
+    on STFusion with the device EGD deciding per layer and per call from the
+    measured masks), config 4 Spikformer B=64."""
+    from catfuse_b200 import hardware
+    from catfuse_b200.network import CTFNetwork
+    from catfuse_b200.sj import spikformer, zoo
+    from catfuse_b200.spikformer_net import CTFSpikformer
+    from catfuse_b200.substitute import substitute, substitute_sf
+    out = {}
+
+    def measure(plan, B, label, flops=None):
+        for _ in range(3):
+            plan.fresh = True
+            plan.run(use_graph=True)
+        ms = max_over_ranks(sum(time_plan(plan, steps, flush)), dev, dist) / steps
+        r = {"samples_per_s": world * B * 1000.0 / ms, "ms_per_step": ms, "per_gpu_batch": B,
+             "steps": steps}
+        if flops:
+            r["conv_tflops_per_s"] = flops / (ms / 1000.0) / 1e12
+        out[label] = r
+        return r
+
+    g = torch.Generator().manual_seed(77)
+    # config 3: Spiking ResNet-18, ImageNet stem, 224x224, B=32
+    B3 = 32
+    net = zoo.init_random_(zoo.build_spiking_resnet18_imagenet(num_classes=1000), 0)
+    calib = torch.randn(8, 3, 224, 224, generator=g).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+    zoo.calibrate_bn_(net, calib)
+    net.eval()
+    x3 = torch.randn(B3, 3, 224, 224, generator=g).to(dev).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+    m3, _ = substitute(net)
+    c3 = CTFNetwork(m3.to(dev), use_sparse=False)
+    p3 = c3.plan_for(x3)
+    p3.x_in.copy_(x3)
+    measure(p3, B3, "spiking_resnet18_224_b32 (config 3, DenseKeep)", _conv_flops(p3))
+    del c3, p3
+    ms3, st3 = substitute_sf(net, T=T_STEPS, force_sparse=True, hwprof=hardware.B200)
+    e3 = CTFNetwork(ms3.to(dev), use_sparse=True)
+    pe3 = e3.plan_for(x3)
+    pe3.x_in.copy_(x3)
+    r = measure(pe3, B3, "spiking_resnet18_224_b32 (config 3, STFusion + device EGD)")
+    r["egd"] = egd_report(pe3)
+    del e3, pe3, x3
+    # config 4: Spikformer, embed 384, 12 heads, 4 blocks, B=64
+    sf = zoo.init_random_(spikformer.build_spikformer_cifar(), 0)
+    calib = torch.randn(16, 3, 32, 32, generator=g).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+    zoo.calibrate_bn_(sf, calib)
+    sf.eval()
+    msf, _ = substitute_sf(sf, T=T_STEPS)
+    csf = CTFSpikformer(msf.to(dev))
+    x4 = torch.randn(BATCH, 3, 32, 32, generator=g).to(dev).unsqueeze(0).repeat(T_STEPS, 1, 1, 1, 1)
+    p4 = csf.plan_for(x4)
+    p4.x_in.copy_(x4)
+    measure(p4, BATCH, "spikformer_b64 (config 4)")
+    return out
+
+
 def conv_roofline(plan, flush, peaks, peak_src):
     """The forward's conv launches replayed alone as one CUDA graph (same
     inputs, same order, L2 flushed before each replay), plus each launch timed
@@ -437,6 +497,7 @@ def main():
             "fp32": {"value": world * B * n_side / (t32 / 1000.0), "steps": n_side,
                      "note": "fp32-faithful: exact integer weight planes, hi+lo stem"}}
         del m32, p32
+        extras["workloads"] = other_workloads(dev, flush, n_side, dist, world)
         if world > 1 and BATCH % world == 0:
             # strong scaling: the global batch of 64 sharded over the ranks
             bs = BATCH // world

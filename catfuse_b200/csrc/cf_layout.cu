@@ -40,6 +40,26 @@ __global__ void pack_kernel(const void* __restrict__ x, int fmt, __half* __restr
   }
 }
 
+// Few channels (C <= 8, Cp <= 32: image inputs): one thread per (t, b, h, w),
+// w fastest so the C plane reads are coalesced; each thread writes its
+// (b, h, w, t) row of Cp halves with 16-byte stores.
+__global__ void pack_small_kernel(const void* __restrict__ x, int fmt, __half* __restrict__ y,
+                                  int T, int B, int C, int H, int W, int Cp) {
+  const int64_t plane = (int64_t)H * W;
+  const int64_t n = (int64_t)T * B * plane;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tb = i / plane, hw = i - tb * plane;
+    const int t = (int)(tb / B), b = (int)(tb - (int64_t)t * B);
+    __align__(16) __half row[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) row[c] = __float2half_rn(0.f);
+    for (int c = 0; c < C; ++c) row[c] = __float2half_rn(ld_f(x, fmt, (tb * C + c) * plane + hw));
+    uint4* dst = reinterpret_cast<uint4*>(y + (((int64_t)b * plane + hw) * T + t) * Cp);
+    for (int q = 0; q < Cp / 8; ++q) dst[q] = reinterpret_cast<const uint4*>(row)[q];
+  }
+}
+
 // y[B][H][W][T][C] -> x[T][B][C][H][W].  grid: (ceil(W/32), ceil(C/32), T*B*H)
 __global__ void unpack_kernel(const __half* __restrict__ y, void* __restrict__ x, int fmt, int T,
                               int B, int C, int H, int W) {
@@ -167,28 +187,46 @@ __global__ void pack_weight_planes_kernel(const float* __restrict__ w, __half* _
   }
 }
 
-// One CTA per (t, b): mean over H*W of x[b][:, :, t, :] into shared memory,
-// then one warp per class computes the fc dot product.
+// kFcRows (t, b) rows per CTA: their means over H*W go to shared memory,
+// then one warp per class reads the class's fc row once for all of them.
+constexpr int kFcRows = 4;
 __global__ void avgpool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
                                   const float* __restrict__ fc_b, float* __restrict__ logits,
                                   int T, int B, int HW, int C, int K) {
-  extern __shared__ float s_mean[];
-  const int t = blockIdx.x % T;
-  const int b = blockIdx.x / T;
+  extern __shared__ float s_mean[];  // [kFcRows][C]
+  const int r0 = blockIdx.x * kFcRows;
+  const int nr = min(kFcRows, T * B - r0);
   const float inv = 1.0f / (float)HW;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+  for (int i = threadIdx.x; i < nr * C; i += blockDim.x) {
+    const int rr = i / C, c = i - rr * C;
+    const int row = r0 + rr;            // row = b * T + t
+    const int b = row / T, t = row - b * T;
     float s = 0.f;
     const __half* p = x + (((int64_t)b * HW) * T + t) * C + c;
-    for (int i = 0; i < HW; ++i) s += __half2float(p[(int64_t)i * T * C]);
-    s_mean[c] = s * inv;
+    for (int j = 0; j < HW; ++j) s += __half2float(p[(int64_t)j * T * C]);
+    s_mean[rr * C + c] = s * inv;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int k = warp; k < K; k += blockDim.x >> 5) {
-    float acc = 0.f;
-    for (int c = lane; c < C; c += 32) acc += s_mean[c] * fc_w[(int64_t)k * C + c];
-    for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) logits[((int64_t)t * B + b) * K + k] = acc + (fc_b ? fc_b[k] : 0.f);
+    float acc[kFcRows];
+#pragma unroll
+    for (int rr = 0; rr < kFcRows; ++rr) acc[rr] = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float wk = fc_w[(int64_t)k * C + c];
+#pragma unroll
+      for (int rr = 0; rr < kFcRows; ++rr)
+        if (rr < nr) acc[rr] += s_mean[rr * C + c] * wk;
+    }
+#pragma unroll
+    for (int rr = 0; rr < kFcRows; ++rr) {
+      float a = acc[rr];
+      for (int off = 16; off; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+      if (lane == 0 && rr < nr) {
+        const int row = r0 + rr, b = row / T, t = row - b * T;
+        logits[((int64_t)t * B + b) * K + k] = a + (fc_b ? fc_b[k] : 0.f);
+      }
+    }
   }
 }
 
@@ -328,6 +366,14 @@ int cf_pack_tbchw(const void* x, int x_fmt, void* y, int64_t T, int64_t B, int64
   if (T * B == 0) return CF_OK;
   if (T * B * H > 0x7FFFFFFF) return fail(CF_ERR_UNSUPPORTED, "T*B*H too large");
   if (int rc = require_sm100()) return rc;
+  if (C <= 8 && Cp <= 32 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    const int64_t n = T * B * H * W;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    pack_small_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, x_fmt, static_cast<__half*>(y), (int)T, (int)B, (int)C, (int)H, (int)W, (int)Cp);
+    return check_launch("pack launch");
+  }
   dim3 grid((unsigned)((W + TB - 1) / TB), (unsigned)((Cp + TB - 1) / TB), (unsigned)(T * B * H));
   pack_kernel<<<grid, dim3(TB, 8), 0, static_cast<cudaStream_t>(stream)>>>(
       x, x_fmt, static_cast<__half*>(y), (int)T, (int)B, (int)C, (int)H, (int)W, (int)Cp);
@@ -381,9 +427,10 @@ int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b, float* lo
   if (!x || !fc_w || !logits) return fail(CF_ERR_INVALID_ARG, "NULL pointer");
   if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || C <= 0 || K <= 0)
     return fail(CF_ERR_INVALID_ARG, "bad shape");
-  if (C * 4 > 48 * 1024) return fail(CF_ERR_UNSUPPORTED, "C too large for the head kernel");
+  if (C * 4 * kFcRows > 48 * 1024) return fail(CF_ERR_UNSUPPORTED, "C too large for the head kernel");
   if (int rc = require_sm100()) return rc;
-  avgpool_fc_kernel<<<(unsigned)(T * B), 256, (size_t)C * 4, static_cast<cudaStream_t>(stream)>>>(
+  avgpool_fc_kernel<<<(unsigned)((T * B + kFcRows - 1) / kFcRows), 256, (size_t)C * 4 * kFcRows,
+                      static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), fc_w, fc_b, logits, (int)T, (int)B, (int)(H * W), (int)C,
       (int)K);
   return check_launch("avgpool_fc launch");

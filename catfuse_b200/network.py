@@ -144,7 +144,9 @@ class NetworkPlan:
         # (hi + lo precision: the parts of the real-valued input side by side,
         # for any kernel size)
         kk_mult = 2 if hi_lo else 1
-        self.im2col = k0 > 1 and (hi_lo or cin * k0 * k0 <= 64)
+        # (few input channels, e.g. images: a k x k stem over 3 channels would
+        # otherwise run k*k tiny K=16 chunks per tile)
+        self.im2col = k0 > 1 and (hi_lo or cin <= 8)
         if self.im2col:
             ho0, wo0 = sspec.output_hw(H, W)
             self.shapes.append((B, ho0, wo0, T, ops.pad16(kk_mult * cin * k0 * k0)))

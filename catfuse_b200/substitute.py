@@ -217,8 +217,18 @@ def substitute_sf(sj_model, T=16, verbose=False, force_sparse=False, hwprof=None
                     for _, m in child.named_modules():
                         if _is_lif(m):
                             done.add(id(m))
-                    setattr(parent, name, cls.from_sj_block(child))
-                    for _ in range(nlif(child)):
+                    blk = cls.from_sj_block(child)
+                    n_rec = nlif(child)
+                    if cls is CTFSpikingBasicBlock:
+                        # the block's first Conv-BN-LIF is routed like any other
+                        # (SparseFlow with the runtime EGD where the policy says so)
+                        fused, pat, shape, backend, K = fuse_conv(child.conv1, child.bn1,
+                                                                  child.sn1)
+                        blk.fused_first = fused
+                        record(cpath + ".conv1", pat, shape, backend, K)
+                        n_rec -= 1
+                    setattr(parent, name, blk)
+                    for _ in range(n_rec):
                         record(cpath, pname, "block", SpatialBackend.DENSE_KEEP, T)
                     break
             else:

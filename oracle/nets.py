@@ -121,7 +121,7 @@ def _resnet18_forward(x, p, sew, stem, record=None, branch_dtype=None, dtype=tor
                 ident = (_conv_bn(xin, p, pre + ".downsample.0", pre + ".downsample.1", stride, 0)
                          if has_ds else xin)
                 if has_ds and branch_dtype is not None:   # storage precision of the branch
-                    ident = ident.to(branch_dtype).float()
+                    ident = ident.to(branch_dtype).to(z2.dtype)
                 s2, v2 = _lif(z2 + ident)
                 if record is not None:
                     record.append((pre + ".sn2", s2, v2))
@@ -138,7 +138,9 @@ def sew_resnet18_forward(x, p, stem="cifar", record=None, dtype=torch.float32):
     return _resnet18_forward(x, p, True, stem, record, None, dtype)
 
 
-def spiking_resnet18_forward(x, p, stem="imagenet", record=None, branch_dtype=None):
+def spiking_resnet18_forward(x, p, stem="imagenet", record=None, branch_dtype=None,
+                             dtype=torch.float32):
     """``branch_dtype`` rounds the Conv-BN downsample branch to that type before
-    the residual add (to mirror a kernel that stores the branch in fp16)."""
-    return _resnet18_forward(x, p, False, stem, record, branch_dtype)
+    the residual add (to mirror a kernel that stores the branch in fp16);
+    ``dtype`` float64 gives the high-precision reference."""
+    return _resnet18_forward(x, p, False, stem, record, branch_dtype, dtype)

@@ -429,3 +429,48 @@ def test_network_device_egd_equals_dense(dev):
     assert torch.equal(a, b)
     plan = sparse.plan_for(xd)
     assert sum(1 for s in plan.steps if getattr(s, "sparse", False)) > 6
+
+
+def _spiking_net_224(B, seed):
+    from catfuse_b200.sj import zoo
+    net = zoo.init_random_(zoo.build_spiking_resnet18_imagenet(num_classes=1000), seed)
+    g = torch.Generator().manual_seed(500 + seed)
+    x = torch.randn(B, 3, 224, 224, generator=g).unsqueeze(0).repeat(4, 1, 1, 1, 1)
+    zoo.calibrate_bn_(net, x)
+    return net.eval(), x
+
+
+def test_spiking_resnet18_224_fp16(dev):
+    """Config 3 shape (Spiking ResNet-18, ImageNet stem 7x7/2 + max-pool,
+    add-before-LIF blocks, 224x224; B=2 to keep the CPU oracle short): every
+    layer, fed its own input, meets the per-layer gates against the oracle at
+    the kernel's operand precision.  (End to end, a single near-threshold
+    flip among the stem's 1.6 M neurons already cascades through the 16 later
+    layers, so the logits are compared per layer rather than at the end.)"""
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import functional
+    net, x = _spiking_net_224(B=2, seed=5)
+    model, stats = optimize(net, device=dev, T=4)
+    assert stats["native_plan"]
+    functional.reset_net(model)
+    logits = model(x.to(dev)).cpu()
+    assert torch.isfinite(logits).all()
+    plan = model.plan_for(x.to(dev))
+    assert plan.shapes[1][1:3] == (112, 112) and plan.shapes[-1][1:3] == (7, 7)
+    assert _teacher_forced_layers(plan, dev) <= 1e-4
+
+
+def test_spiking_resnet18_224_fp32_mode(dev):
+    """Config 3 shape in the fp32-faithful mode: every layer, fed its own
+    input, against an fp64 restatement of the layer -- flips only within 1e-5
+    of the threshold, v within 1e-4 (the z-only downsample branch enters the
+    add-before-LIF epilogue from the fp16 activation layout, as the oracle
+    restatement reads it)."""
+    from catfuse_b200 import optimize
+    from catfuse_b200.sj import functional
+    net, x = _spiking_net_224(B=2, seed=6)
+    model, _ = optimize(net, device=dev, T=4, precision="fp32")
+    functional.reset_net(model)
+    model(x.to(dev))
+    plan = model.plan_for(x.to(dev))
+    assert _teacher_forced_fp64(plan) <= 1e-4
