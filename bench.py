@@ -325,14 +325,17 @@ def conv_roofline(plan, flush, peaks, peak_src):
     from catfuse_b200 import ops
 
     def launch(st):
-        ident = plan.acts[st.identity] if st.identity is not None else None
-        mode = "z_only" if st.lif is None else (st.res_mode if ident is not None else "none")
-        ops.conv_bn_lif(plan.acts[st.src], st.wp, st.scale, st.shift, st.stride, st.pad,
-                        identity=ident if st.lif is not None else None, res_mode=mode,
-                        v_in=None, v_out=st.v, lif=st.lif or ops.LIFConfig(),
-                        out=plan.acts[st.dst], precision=st.prec)
+        plan.conv_launch(st, True)
 
-    convs = [st for st in plan.steps if isinstance(st, ConvStep)]
+    def layer_flops(st):
+        fl = 0.0
+        for c in (st, st.dual) if st.dual is not None else (st,):
+            b_, ho, wo, t_, co = plan.shapes[c.dst]
+            spec = c.native.spec
+            fl += 2.0 * t_ * b_ * ho * wo * co * spec.in_channels * spec.kernel_size ** 2
+        return fl
+
+    convs = [st for st in plan.steps if isinstance(st, ConvStep) and not st.fused]
 
     def conv_launches():
         for st in convs:
@@ -361,9 +364,7 @@ def conv_roofline(plan, flush, peaks, peak_src):
     peak = peaks["bf16_tflops"]
     per_layer = []
     for st in convs:
-        b_, ho, wo, t_, co = plan.shapes[st.dst]
-        spec = st.native.spec
-        fl = 2.0 * t_ * b_ * ho * wo * co * spec.in_channels * spec.kernel_size ** 2
+        fl = layer_flops(st)
         g1 = torch.cuda.CUDAGraph()          # one launch, replayed (no host overhead timed)
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.graph(g1, stream=side):
@@ -380,7 +381,8 @@ def conv_roofline(plan, flush, peaks, peak_src):
             ts.append((a, b))
         torch.cuda.synchronize()
         us = 1000.0 * statistics.mean(a.elapsed_time(b) for a, b in ts)
-        per_layer.append({"layer": st.name, "us": round(us, 2),
+        per_layer.append({"layer": st.name + ("+" + st.dual.name.split(".")[-1] if st.dual else ""),
+                          "us": round(us, 2),
                           "tflops": round(fl / us / 1e6, 1),
                           "frac": round(fl / us / 1e6 / peak, 3)})
     flops = _conv_flops(plan)
@@ -388,8 +390,8 @@ def conv_roofline(plan, flush, peaks, peak_src):
     return {"bound": "tensor", "achieved": achieved, "peak": peak,
             "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": _traffic_from_profiles(), "peak_source": f"{peak_src} bf16_tflops (burst)",
-            "kernel": "conv_t_kernel / conv_bn_lif_kernel (the 20 conv launches of one "
-                      "forward, replayed as one CUDA graph, L2 flushed before each replay)",
+            "kernel": "conv_t_kernel / conv_bn_lif_kernel (the conv launches of one forward, "
+                      "replayed as one CUDA graph, L2 flushed before each replay)",
             "flops_per_forward": flops, "conv_ms_per_forward": conv_ms_fwd,
             "launches_per_forward": len(convs), "per_layer": per_layer}
 

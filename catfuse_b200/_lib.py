@@ -67,6 +67,9 @@ SIGNATURES = {
     "cf_pack_conv_weight_split": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "cf_pack_im2col_split": (_INT, [_P, _INT, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                     _I64, _P]),
+    "cf_conv_bn_lif_dual": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                   _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _INT,
+                                   _INT, _P]),
     "cf_conv_bn_lif_egd": (_INT, [_P, _P, _P, _P, _P, _INT, _P, _P, _P, _P, _I64, _I64, _I64,
                                   _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _INT,
                                   _INT, _F, _P]),

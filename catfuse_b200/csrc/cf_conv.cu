@@ -203,7 +203,8 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
                      int64_t W, int64_t Cin_p, int64_t Cout, int64_t KH, int64_t KW,
                      int64_t stride, int64_t pad, float tau, float v_th, float v_reset,
                      int hard_reset, int decay_input, int wparts, cudaStream_t stream,
-                     float egd_max_active_frac = -1.f) {
+                     float egd_max_active_frac = -1.f, int64_t co_split = -1,
+                     void* out2 = nullptr, const float* v_in2 = nullptr, float* v_out2 = nullptr) {
   if (!x || !wp || !out) return fail(CF_ERR_INVALID_ARG, "x, wp and out must not be NULL");
   if (T <= 0 || B <= 0 || H <= 0 || W <= 0 || Cin_p <= 0 || Cout <= 0 || KH <= 0 || KW <= 0 ||
       stride <= 0 || pad < 0)
@@ -303,6 +304,20 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   args.shift = shift;
   args.identity = static_cast<const __half*>(identity);
   args.out = static_cast<__half*>(out);
+  args.co_split = co_split >= 0 ? (int)co_split : (int)Cout;
+  args.out2 = static_cast<__half*>(out2);
+  args.v_in2 = v_in2;
+  args.v_out2 = v_out2;
+  if (co_split >= 0) {
+    if (!g.tmode || co_split % g.BN || co_split <= 0 || co_split >= Cout || !out2 ||
+        res_mode != CF_RES_NONE || tile_mask || wparts != 1)
+      return fail(CF_ERR_UNSUPPORTED,
+                  "dual output needs the channel-major kernel, a split on an output-channel "
+                  "tile (multiple of %d), no residual, no mask and fp16 weights", g.BN);
+    const void* p2[] = {out2, v_in2, v_out2};
+    for (const void* p : p2)
+      if (p && !al16(p)) return fail(CF_ERR_UNSUPPORTED, "tensor pointers must be 16-byte aligned");
+  }
   args.tile_mask = tile_mask;
   args.T = (int)T;
   args.B = (int)B; args.Ho = (int)Ho; args.Wo = (int)Wo;
@@ -375,6 +390,7 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
     args.tcount = (int)((T - t0) < kMaxTP ? (T - t0) : kMaxTP);
     args.v_in = (t0 == 0) ? v_in : v_out;
     args.v_out = v_out;
+    args.v_in2 = (t0 == 0) ? v_in2 : v_out2;
     if (int rc = dispatch(g, res_mode, fast, tmA, tmB, args, grid, stream)) return rc;
     args.drop_load = 0;
   }
@@ -479,6 +495,20 @@ int cf_conv_bn_lif_egd(const void* x, const void* wp, const float* scale, const 
                           B, H, W, Cin_p, Cout, KH, KW, stride, pad, tau, v_threshold, v_reset,
                           hard_reset, decay_input, 1, static_cast<cudaStream_t>(stream),
                           max_active_frac);
+}
+
+int cf_conv_bn_lif_dual(const void* x, const void* wp, const float* scale, const float* shift,
+                        const float* v_in, float* v_out, void* out, const float* v_in2,
+                        float* v_out2, void* out2, int64_t Cout1, int64_t T, int64_t B, int64_t H,
+                        int64_t W, int64_t Cin_p, int64_t Cout, int64_t KH, int64_t KW,
+                        int64_t stride, int64_t pad, float tau, float v_threshold, float v_reset,
+                        int hard_reset, int decay_input, void* stream) {
+  if (Cout1 <= 0 || Cout1 >= Cout) return fail(CF_ERR_INVALID_ARG, "need 0 < Cout1 < Cout");
+  if (T > 8 && !v_out2) return fail(CF_ERR_INVALID_ARG, "T > 8 needs v_out2 to carry the membrane");
+  return conv_bn_lif_impl(x, wp, scale, shift, nullptr, CF_RES_NONE, v_in, v_out, out, nullptr, T,
+                          B, H, W, Cin_p, Cout, KH, KW, stride, pad, tau, v_threshold, v_reset,
+                          hard_reset, decay_input, 1, static_cast<cudaStream_t>(stream), -1.f,
+                          Cout1, out2, v_in2, v_out2);
 }
 
 int cf_conv_bn_lif_planes(const void* x, const void* wq, const float* scale, const float* shift,

@@ -71,6 +71,13 @@ struct ConvArgs {
   float* v_out;
   __half* out;
   const uint32_t* tile_mask;
+  // dual output (channel-major kernel): channels [co_split, Cout) go to out2 /
+  // v_in2 / v_out2 (a second conv sharing the input and the LIF parameters);
+  // co_split = Cout for single-output launches
+  __half* out2;
+  const float* v_in2;
+  float* v_out2;
+  int co_split;
   int T;        // total time steps (layout stride)
   int t0;       // first step of this launch
   int tcount;   // steps in this launch (<= TP)
@@ -706,6 +713,15 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
                           RES == CF_RES_IAND_POST);
   constexpr bool kLif = (RES != CF_RES_Z_ONLY);
   constexpr bool full_t = FULLT;  // all TP steps valid: straight-line recurrences
+  // Dual-output launches: output channels from co_split on belong to a second
+  // conv (its own out / v buffers, Cout - co_split channels wide).
+  const bool second = co_base >= a.co_split;
+  __half* const outp = second ? a.out2 : a.out;
+  const float* const vinp = second ? a.v_in2 : a.v_in;
+  float* const voutp = second ? a.v_out2 : a.v_out;
+  const int cstride = second ? a.Cout - a.co_split : a.co_split;
+  const int cbase = second ? co_base - a.co_split : co_base;
+  const int cown = second ? co - a.co_split : co;
   const int h = MT == 128 ? 0 : (lane >> 4);
   const int cl = MT == 128 ? lane : (lane & 15);
   const int p0 = (col0 + 32 * h) / TP;
@@ -723,7 +739,7 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
     const int b = bt * a.Bb + (p >> (a.lwb + a.lhb));
     rok[i] = wo < a.Wo && ho < a.Ho && b < a.B && t < a.tcount;
     const int64_t pix = ((int64_t)b * a.Ho + ho) * a.Wo + wo;
-    row_off[i] = (pix * a.T + a.t0 + t) * a.Cout + co_base;
+    row_off[i] = (pix * a.T + a.t0 + t) * cstride + cbase;
   }
 
   // Post-LIF combines: fetch this lane's identity rows now so their latency
@@ -791,7 +807,7 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
   }
   if constexpr (kLif) {
 #pragma unroll
-    for (int pp = 0; pp < PP; ++pp) v[pp] = (a.v_in && ok[pp]) ? a.v_in[pix[pp] * a.Cout + co] : 0.f;
+    for (int pp = 0; pp < PP; ++pp) v[pp] = (vinp && ok[pp]) ? vinp[pix[pp] * cstride + cown] : 0.f;
   }
 
   uint8_t* hbase = stage + cl * 2;
@@ -820,10 +836,10 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
     if (kLif) v[pp] = vv;
   }
   if constexpr (kLif) {
-    if (a.v_out) {
+    if (voutp) {
 #pragma unroll
       for (int pp = 0; pp < PP; ++pp)
-        if (ok[pp]) a.v_out[pix[pp] * a.Cout + co] = v[pp];
+        if (ok[pp]) voutp[pix[pp] * cstride + cown] = v[pp];
     }
   }
   __syncwarp();
@@ -849,7 +865,7 @@ __device__ __forceinline__ void epi_chunk_t(const ConvArgs& a, const float (&r)[
         }
       }
     }
-    uint4* dst = reinterpret_cast<uint4*>(a.out + row_off[i]);
+    uint4* dst = reinterpret_cast<uint4*>(outp + row_off[i]);
 #pragma unroll
     for (int k = 0; k < NQ; ++k) dst[k] = o4[k];
   }

@@ -62,6 +62,13 @@ class ConvStep:
     pad: int = 0
     im2col: bool = False
     prec: str = "fp16"            # operand precision of this launch (ops.PRECISIONS)
+    # dual launch: this conv also computes `dual` (the block's downsample) in
+    # the same kernel (concatenated weight rows); the partner is skipped
+    dual: Optional["ConvStep"] = None
+    fused: bool = False
+    dual_wp: Optional[torch.Tensor] = None
+    dual_scale: Optional[torch.Tensor] = None
+    dual_shift: Optional[torch.Tensor] = None
 
 
 @dataclass
@@ -173,6 +180,7 @@ class NetworkPlan:
                                        _lif_of(pat) if lif else None, sparse, prec=prec))
             return dst
 
+        pairs = []   # (conv1, downsample) steps of SEW blocks
         if self.im2col:
             b_, h_, w_, t_, c_ = self.shapes[0]
             self.shapes.append((b_, h_, w_, t_, sspec.out_channels))
@@ -203,6 +211,8 @@ class NetworkPlan:
                 h1 = add_conv(nm + ".conv1", first, x_in)
                 if kind == "sew":
                     ident = add_conv(nm + ".downsample", ds, x_in) if ds is not None else x_in
+                    if ds is not None:
+                        pairs.append((self.steps[-2], self.steps[-1]))
                     cur = add_conv(nm + ".conv2", second, h1, ident, cnf)
                 else:
                     ident = x_in
@@ -239,16 +249,85 @@ class NetworkPlan:
                     cin_p = self.shapes[st.src][-1]
                     g = ops.conv_geometry(t_, b_, ho, wo, co, cin_p, st.stride, True)
                     st.mask = torch.zeros(g["n_mtiles"], dtype=torch.int32, device=self.device)
+        for first, ds in pairs:
+            self._try_dual(first, ds)
         from .hardware import detect_hardware
         frac = detect_hardware().egd_max_active_frac
         self.egd_frac = frac if frac >= 0 else 1.0
         self.fresh = True
         self._graphs = {}
 
+    def _try_dual(self, first: ConvStep, ds: ConvStep) -> None:
+        """Run a SEW block's 1x1 stride-s downsample in the launch of its 3x3
+        stride-s first conv (same input; the downsample's weights at the
+        centre tap) when both are plain fp16 LIF convs on the channel-major
+        kernel."""
+        fs, dsp = first.native.spec, ds.native.spec
+        c1, c2 = fs.out_channels, dsp.out_channels
+        cin_p = self.shapes[first.src][-1]
+        ok = (first.prec == ds.prec == "fp16" and not first.sparse and not ds.sparse
+              and first.lif is not None and ds.lif is not None and first.lif == ds.lif
+              and first.identity is None and ds.identity is None
+              and fs.kernel_size == 3 and fs.padding == 1 and dsp.kernel_size == 1
+              and dsp.padding == 0 and fs.stride == dsp.stride and first.src == ds.src
+              and (c1 + c2) % 128 == 0 and c1 % 128 == 0 and ops.planes_ok(c1 + c2, cin_p))
+        if not ok:
+            return
+        dev = self.device
+        w1 = first.native.params.weight.detach().float().to(dev)
+        w2 = ds.native.params.weight.detach().float().to(dev)
+        w = torch.zeros((c1 + c2, w1.shape[1], 3, 3), dtype=torch.float32, device=dev)
+        w[:c1] = w1
+        w[c1:, :, 1, 1] = w2[:, :, 0, 0]
+        first.dual_wp = ops.pack_conv_weight(w, cin_p)
+        parts = []
+        for st, c in ((first, c1), (ds, c2)):
+            sc = torch.ones(c, device=dev) if st.scale is None else st.scale.float()
+            sh = torch.zeros(c, device=dev) if st.shift is None else st.shift.float()
+            parts.append((sc, sh))
+        first.dual_scale = torch.cat([parts[0][0], parts[1][0]]).contiguous()
+        first.dual_shift = torch.cat([parts[0][1], parts[1][1]]).contiguous()
+        first.dual = ds
+        ds.fused = True
+
+    def conv_launch(self, st: ConvStep, fresh: bool) -> None:
+        """The kernel launch of one conv step (nothing for a step whose work
+        rides in its partner's dual launch)."""
+        if st.fused:
+            return
+        if st.dual is not None:
+            ds = st.dual
+            ops.conv_bn_lif_dual(self.acts[st.src], st.dual_wp, st.dual_scale, st.dual_shift,
+                                 st.native.spec.out_channels, st.stride, st.pad,
+                                 v_in=None if fresh else st.v, v_out=st.v, out=self.acts[st.dst],
+                                 v_in2=None if fresh else ds.v, v_out2=ds.v,
+                                 out2=self.acts[ds.dst], lif=st.lif)
+            return
+        spec = st.native.spec
+        if st.sparse:
+            ops.prescan_conv_tiles(self.acts[st.src], spec.out_channels, spec.kernel_size,
+                                   spec.kernel_size, spec.stride, spec.padding,
+                                   mask_out=st.mask, egd=True)
+        ident = self.acts[st.identity] if st.identity is not None else None
+        if st.lif is None:
+            ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
+                            st.pad, res_mode="z_only", out=self.acts[st.dst],
+                            precision=st.prec)
+        else:
+            ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
+                            st.pad, identity=ident,
+                            res_mode=st.res_mode if ident is not None else "none",
+                            v_in=None if fresh else st.v, v_out=st.v,
+                            tile_mask=st.mask if st.sparse else None, lif=st.lif,
+                            out=self.acts[st.dst], precision=st.prec,
+                            egd_max_active_frac=self.egd_frac if st.sparse else None)
+
     # ---- execution ---------------------------------------------------------
     def launches(self) -> int:
         n = 2  # pack + head
         for st in self.steps:
+            if isinstance(st, ConvStep) and st.fused:
+                continue
             n += 1 + (1 if isinstance(st, ConvStep) and st.sparse else 0)
         return n
 
@@ -265,26 +344,8 @@ class NetworkPlan:
         for st in self.steps:
             if isinstance(st, PoolStep):
                 ops.maxpool_bhwtc(self.acts[st.src], st.k, st.s, st.p, out=self.acts[st.dst])
-                continue
-            b_, h_, w_, t_, c_ = self.shapes[st.src]
-            spec = st.native.spec
-            if st.sparse:
-                ops.prescan_conv_tiles(self.acts[st.src], spec.out_channels, spec.kernel_size,
-                                       spec.kernel_size, spec.stride, spec.padding,
-                                       mask_out=st.mask, egd=True)
-            ident = self.acts[st.identity] if st.identity is not None else None
-            if st.lif is None:
-                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
-                                st.pad, res_mode="z_only", out=self.acts[st.dst],
-                                precision=st.prec)
             else:
-                ops.conv_bn_lif(self.acts[st.src], st.wp, st.scale, st.shift, st.stride,
-                                st.pad, identity=ident,
-                                res_mode=st.res_mode if ident is not None else "none",
-                                v_in=None if fresh else st.v, v_out=st.v,
-                                tile_mask=st.mask if st.sparse else None, lif=st.lif,
-                                out=self.acts[st.dst], precision=st.prec,
-                                egd_max_active_frac=self.egd_frac if st.sparse else None)
+                self.conv_launch(st, fresh)
         ops.avgpool_fc(self.acts[self.final], self.fc_w, self.fc_b, out=self.logits)
 
     def run(self, use_graph: bool = True):

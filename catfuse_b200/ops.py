@@ -22,7 +22,7 @@ __all__ = [
     "conv_geometry", "prescan", "prescan_conv_tiles", "conv_chunk", "avgpool_fc", "maxpool_bhwtc",
     "pad16", "SPIKE_FORMATS", "RES_MODES", "PRECISIONS", "pack_conv_weight_split",
     "pack_im2col_split", "im2col_weight_split", "split_prescale", "check_device_error",
-    "set_wait_limit", "token_mean_lif_fc",
+    "set_wait_limit", "token_mean_lif_fc", "conv_bn_lif_dual",
 ]
 
 # Operand precision of the fused conv: "fp16" = fp16 weights (spikes are exact
@@ -602,3 +602,26 @@ def token_mean_lif_fc(x: torch.Tensor, fc_w: torch.Tensor, fc_b: Optional[torch.
     _lib.call("cf_token_mean_lif_fc", x.data_ptr(), _ptr(v_in), _ptr(v_out), fc_w.data_ptr(),
               _ptr(fc_b), out.data_ptr(), T, B, N, C, K, *lif.args(), _stream())
     return out
+
+
+def conv_bn_lif_dual(x: torch.Tensor, wp: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                     Cout1: int, stride: int, pad: int, v_in=None, v_out=None, out=None,
+                     v_in2=None, v_out2=None, out2=None, lif: LIFConfig = _DEFAULT_LIF):
+    """Two convs over x[B,H,W,T,Cin_p] in one launch (cf_conv_bn_lif_dual):
+    weight rows [0, Cout1) -> out, [Cout1, Cout) -> out2.  Returns (out, out2)."""
+    _need(x, "x", torch.float16)
+    _need(wp, "wp", torch.float16)
+    B, H, W, T, Cin_p = x.shape
+    Cout, KH, KW, Cw = wp.shape
+    if Cw != Cin_p:
+        raise ValueError("weight / activation channel mismatch")
+    Ho = (H + 2 * pad - KH) // stride + 1
+    Wo = (W + 2 * pad - KW) // stride + 1
+    if out is None:
+        out = torch.empty((B, Ho, Wo, T, Cout1), dtype=torch.float16, device=x.device)
+    if out2 is None:
+        out2 = torch.empty((B, Ho, Wo, T, Cout - Cout1), dtype=torch.float16, device=x.device)
+    _lib.call("cf_conv_bn_lif_dual", x.data_ptr(), wp.data_ptr(), _ptr(scale), _ptr(shift),
+              _ptr(v_in), _ptr(v_out), out.data_ptr(), _ptr(v_in2), _ptr(v_out2), out2.data_ptr(),
+              int(Cout1), T, B, H, W, Cin_p, Cout, KH, KW, stride, pad, *lif.args(), _stream())
+    return out, out2

@@ -269,6 +269,24 @@ CF_API int cf_conv_bn_lif_egd(const void* x, const void* wp, const float* scale,
                               int hard_reset, int decay_input, float max_active_frac,
                               void* stream);
 
+/* Two convolutions over the same input in one launch: output channels
+ * [0, Cout1) are written to out / v_in / v_out ([B][Ho][Wo][T][Cout1],
+ * [B][Ho][Wo][Cout1]) and [Cout1, Cout) to out2 / v_in2 / v_out2 (Cout - Cout1
+ * channels wide); wp / scale / shift hold both convs' rows.  A SEW block's
+ * 1x1 stride-s downsample conv (+BN+LIF) rides along its 3x3 stride-s first
+ * conv this way: its weights sit at the centre tap of a 3x3 slab (the centre
+ * tap of a pad-1 3x3 conv reads exactly the pixel a pad-0 1x1 conv reads), so
+ * the input is read once for both (catfuse/patterns.py:676-715: conv1 and
+ * downsample of the same block).  Channel-major shapes only, Cout1 a multiple
+ * of the output-channel tile, no residual, no mask, fp16 weights. */
+CF_API int cf_conv_bn_lif_dual(const void* x, const void* wp, const float* scale,
+                               const float* shift, const float* v_in, float* v_out, void* out,
+                               const float* v_in2, float* v_out2, void* out2, int64_t Cout1,
+                               int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin_p,
+                               int64_t Cout, int64_t KH, int64_t KW, int64_t stride,
+                               int64_t pad, float tau, float v_threshold, float v_reset,
+                               int hard_reset, int decay_input, void* stream);
+
 /* Extended-precision variant of cf_conv_bn_lif: the weight is carried as two
  * fp16 parts, wp2[Cout][KH][KW][2][Cin_p] = {hi, lo} (cf_pack_conv_weight_split),
  * and every (tap, channel chunk) issues the hi and the lo MMAs into the same

@@ -474,3 +474,31 @@ def test_spiking_resnet18_224_fp32_mode(dev):
     model(x.to(dev))
     plan = model.plan_for(x.to(dev))
     assert _teacher_forced_fp64(plan) <= 1e-4
+
+
+def test_dual_launch_downsample_bit_identical(dev, monkeypatch):
+    """SEW blocks' 1x1/s2 downsample computed inside the first conv's launch
+    (cf_conv_bn_lif_dual) gives the same spikes, membranes and logits bit for
+    bit as two separate launches."""
+    from catfuse_b200 import optimize
+    from catfuse_b200.network import ConvStep, NetworkPlan
+    from catfuse_b200.sj import functional
+    net, x = _sew_net(B=8, seed=3)
+    xd = x.to(dev)
+    m1, _ = optimize(net, device=dev, T=4)
+    functional.reset_net(m1)
+    a = m1(xd)
+    p1 = m1.plan_for(xd)
+    assert sum(1 for st in p1.steps if isinstance(st, ConvStep) and st.dual is not None) == 3
+    monkeypatch.setattr(NetworkPlan, "_try_dual", lambda self, f, d: None)
+    m2, _ = optimize(net, device=dev, T=4)
+    functional.reset_net(m2)
+    b = m2(xd)
+    p2 = m2.plan_for(xd)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    for s1, s2 in zip(p1.steps, p2.steps):
+        if isinstance(s1, ConvStep):
+            assert torch.equal(p1.acts[s1.dst], p2.acts[s2.dst]), s1.name
+            if s1.v is not None:
+                assert torch.equal(s1.v, s2.v), s1.name
