@@ -187,15 +187,16 @@ __global__ void pack_weight_planes_kernel(const float* __restrict__ w, __half* _
   }
 }
 
-// kFcRows (t, b) rows per CTA: their means over H*W go to shared memory,
-// then one warp per class reads the class's fc row once for all of them.
+// `rows` (t, b) rows per CTA (1 for small heads, kFcRows when there are many
+// classes): their means over H*W go to shared memory, then one warp per class
+// reads the class's fc row once for all of them.
 constexpr int kFcRows = 4;
 __global__ void avgpool_fc_kernel(const __half* __restrict__ x, const float* __restrict__ fc_w,
                                   const float* __restrict__ fc_b, float* __restrict__ logits,
-                                  int T, int B, int HW, int C, int K) {
-  extern __shared__ float s_mean[];  // [kFcRows][C]
-  const int r0 = blockIdx.x * kFcRows;
-  const int nr = min(kFcRows, T * B - r0);
+                                  int T, int B, int HW, int C, int K, int rows) {
+  extern __shared__ float s_mean[];  // [rows][C]
+  const int r0 = blockIdx.x * rows;
+  const int nr = min(rows, T * B - r0);
   const float inv = 1.0f / (float)HW;
   for (int i = threadIdx.x; i < nr * C; i += blockDim.x) {
     const int rr = i / C, c = i - rr * C;
@@ -429,10 +430,11 @@ int cf_avgpool_fc(const void* x, const float* fc_w, const float* fc_b, float* lo
     return fail(CF_ERR_INVALID_ARG, "bad shape");
   if (C * 4 * kFcRows > 48 * 1024) return fail(CF_ERR_UNSUPPORTED, "C too large for the head kernel");
   if (int rc = require_sm100()) return rc;
-  avgpool_fc_kernel<<<(unsigned)((T * B + kFcRows - 1) / kFcRows), 256, (size_t)C * 4 * kFcRows,
+  const int rows = K >= 64 ? kFcRows : 1;
+  avgpool_fc_kernel<<<(unsigned)((T * B + rows - 1) / rows), 256, (size_t)C * 4 * rows,
                       static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), fc_w, fc_b, logits, (int)T, (int)B, (int)(H * W), (int)C,
-      (int)K);
+      (int)K, rows);
   return check_launch("avgpool_fc launch");
 }
 

@@ -86,13 +86,18 @@ __global__ void __launch_bounds__(kPrescanThreads)
                    ((reinterpret_cast<uintptr_t>(x) + (uintptr_t)(base * esz)) % 16 == 0);
   const int ngrp = vec ? HW / 8 : HW;
   const __half2 thr2 = __half2half2(__float2half_rd(thr));  // |h| > thr  <=>  |h| > rd_half(thr)
-  for (int grp = threadIdx.x; grp < ngrp; grp += blockDim.x) {
+  // Small planes: csplit subsets of the threads share the pixel groups, each
+  // taking every csplit-th channel (their partial bits meet in the atomicOr).
+  const int csplit = ngrp >= (int)blockDim.x ? 1 : max(1, min(4, (int)blockDim.x / ngrp));
+  const int tpc = ngrp >= (int)blockDim.x ? (int)blockDim.x : ngrp;  // threads per subset
+  const int sub = (int)threadIdx.x / tpc;
+  for (int grp = (int)threadIdx.x - sub * tpc; sub < csplit && grp < ngrp; grp += tpc) {
     const int px0 = vec ? grp * 8 : grp;
     const int npx = vec ? 8 : 1;
     uint32_t bits[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
     // nonzero-pixel mask of the current channel group, folded into bits[]
     // when the group changes (group bits are per GS channels)
-    int g_cur = c0 / GS;
+    int g_cur = (c0 + sub) / GS;
     uint32_t nzpix = 0;
     auto fold = [&]() {
       if (!nzpix) return;
@@ -101,13 +106,14 @@ __global__ void __launch_bounds__(kPrescanThreads)
       for (int j = 0; j < 8; ++j) bits[j] |= ((nzpix >> j) & 1u) ? gbit : 0u;
       nzpix = 0;
     };
-    for (int c = c0; c < c1; c += 4) {
-      uint32_t nzf[4];  // bit j: pixel px0 + j of channel c + u has |x| > thr
+    for (int c = c0 + sub; c < c1; c += 4 * csplit) {
+      uint32_t nzf[4];  // bit j: pixel px0 + j of channel c + u * csplit has |x| > thr
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         nzf[u] = 0u;
-        if (c + u >= c1) continue;
-        const int64_t e0 = base + (int64_t)(c + u - c0) * plane + px0;
+        const int ch = c + u * csplit;
+        if (ch >= c1) continue;
+        const int64_t e0 = base + (int64_t)(ch - c0) * plane + px0;
         if (vec && fmt == CF_FMT_F16) {
           const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(x) + e0));
           const uint32_t w[4] = {q.x, q.y, q.z, q.w};
@@ -143,8 +149,9 @@ __global__ void __launch_bounds__(kPrescanThreads)
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        if (c + u >= c1) continue;
-        const int g = (c + u) / GS;
+        const int ch = c + u * csplit;
+        if (ch >= c1) continue;
+        const int g = ch / GS;
         if (g != g_cur) {
           fold();
           g_cur = g;

@@ -67,6 +67,9 @@ def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--only", choices=["lif", "prescan", "sweep"], default=None,
+                    help="run one group: the LIF family, the two prescans once each on the "
+                         "config-2 input (s = 0.9), or the SparseFlow sweep")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
     peak, src = _peak()
@@ -79,6 +82,17 @@ def main(argv=None):
         rows.append((name, us, nbytes / 1e6, gbs, gbs / peak))
         print(f"{name:58s} {us:8.1f} us {nbytes / 1e6:8.1f} MB {gbs:7.0f} GB/s "
               f"{gbs / peak:6.1%} of {src} {peak:.0f}")
+
+    if args.only == "prescan":
+        T, B, C, H, W = 4, 32, 256, 28, 28
+        x = workloads.block_sparse_spikes(T, B, C, H, W, 0.9, seed=900).to(dev)
+        xp = ops.pack_tbchw(x)
+        us = _time(lambda: ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1), args.reps, flush)
+        report("prescan_conv_tiles  x [32,28,28,4,256] fp16  s=0.9", us, xp.numel() * 2)
+        xr = x.reshape(T * B, C, H, W).half().contiguous()
+        us = _time(lambda: ops.prescan(xr, 3, 1, 1, 8, 8, 32), args.reps, flush)
+        report("prescan (reference geometry) x [128,256,28,28] fp16", us, xr.numel() * 2)
+        return 0
 
     # ---- config 0: LIF family ---------------------------------------------
     T, B, C, H, W = 4, 32, 128, 32, 32
@@ -94,6 +108,8 @@ def main(argv=None):
     z2 = torch.randn(T, B, C, H, W, generator=g).to(dev)
     us = _time(lambda: ops.add_lif(z, z2, spike_dtype=torch.float16), args.reps, flush)
     report("add_lif  2 x fp32 -> spikes fp16", us, T * N * 8 + T * N * 2 + 4 * N)
+    if args.only == "lif":
+        return 0
 
     # ---- config 2: prescan and sparse conv sweep -----------------------------
     T, B, C, H, W = 4, 32, 256, 28, 28
