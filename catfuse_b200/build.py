@@ -70,9 +70,16 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
     BUILD_DIR.mkdir(exist_ok=True)
     extra = list(extra or [])
     srcs = _sources()
-    jobs = jobs or min(len(srcs), os.cpu_count() or 4)
-    with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
-        objs = list(ex.map(lambda s: _compile(s, extra), srcs))
+    objs = [BUILD_DIR / (s.stem + ".o") for s in srcs]
+    # an object is rebuilt when it is older than its source or any shared header
+    hdr = max((p.stat().st_mtime for p in _deps() if p.suffix != ".cu"), default=0.0)
+    stale = [s for s, o in zip(srcs, objs)
+             if force or extra or not o.exists()
+             or o.stat().st_mtime < max(s.stat().st_mtime, hdr)]
+    if stale:
+        jobs = jobs or min(len(stale), os.cpu_count() or 4)
+        with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
+            list(ex.map(lambda s: _compile(s, extra), stale))
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [_nvcc(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
     res = subprocess.run(cmd, capture_output=True, text=True)
