@@ -73,6 +73,9 @@ SIGNATURES = {
     "cf_conv_bn_lif_egd": (_INT, [_P, _P, _P, _P, _P, _INT, _P, _P, _P, _P, _I64, _I64, _I64,
                                   _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _INT,
                                   _INT, _F, _P]),
+    "cf_conv_bn_lif_egd_noalloc": (_INT, [_P, _P, _P, _P, _P, _INT, _P, _P, _P, _I64, _I64,
+                                          _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F,
+                                          _F, _F, _INT, _INT, _F, _P]),
     "cf_conv_bn_lif_planes": (_INT, [_P, _P, _P, _P, _P, _INT, _P, _P, _P, _I64, _I64, _I64,
                                      _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _F, _INT,
                                      _INT, _P]),

@@ -269,6 +269,33 @@ CF_API int cf_conv_bn_lif_egd(const void* x, const void* wp, const float* scale,
                               int hard_reset, int decay_input, float max_active_frac,
                               void* stream);
 
+/* cf_conv_bn_lif_egd with its prescan, for callers that cannot allocate
+ * device memory (a host framework whose allocator owns the device and passes
+ * in only a call's tensors, or a hot path under a no-allocation rule): it
+ * runs cf_prescan_conv_tiles (dense chunk) into a mask array that this
+ * library holds in device memory, then cf_conv_bn_lif_egd on those masks.
+ * No counterpart in the reference (its SparseFlow allocates the prescan's
+ * outputs with torch on every call).
+ *   - Limit: at most 65536 M tiles (cf_conv_geometry_ex with flags = 1, out[4]);
+ *     larger shapes return CF_ERR_UNSUPPORTED.  The array takes 256 KB on
+ *     every GPU that loads the library, until the process exits.
+ *   - It calls no cudaMalloc / cudaFree.  Its first call on a device looks up
+ *     the array's device address (cudaGetSymbolAddress) with that device
+ *     current; make that first call before any stream capture.
+ *   - Every call shares the one array: calls whose kernels overlap on the GPU
+ *     (different streams without ordering) race on it.  Calls ordered on one
+ *     stream are safe; the prescan clears the masks it uses on each call.
+ * Arguments as cf_conv_bn_lif_egd without tile_mask; the result is bit for
+ * bit that of cf_prescan_conv_tiles + cf_conv_bn_lif_egd. */
+CF_API int cf_conv_bn_lif_egd_noalloc(const void* x, const void* wp, const float* scale,
+                                      const float* shift, const void* identity, int res_mode,
+                                      const float* v_in, float* v_out, void* out,
+                                      int64_t T, int64_t B, int64_t H, int64_t W, int64_t Cin_p,
+                                      int64_t Cout, int64_t KH, int64_t KW, int64_t stride,
+                                      int64_t pad, float tau, float v_threshold, float v_reset,
+                                      int hard_reset, int decay_input, float max_active_frac,
+                                      void* stream);
+
 /* Two convolutions over the same input in one launch: output channels
  * [0, Cout1) are written to out / v_in / v_out ([B][Ho][Wo][T][Cout1],
  * [B][Ho][Wo][Cout1]) and [Cout1, Cout) to out2 / v_in2 / v_out2 (Cout - Cout1
