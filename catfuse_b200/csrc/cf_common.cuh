@@ -152,6 +152,18 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+// Programmatic dependent launch.  griddep_wait blocks until the grid this
+// launch depends on has completed and its memory is visible (a no-op when the
+// kernel was launched without the programmatic-serialisation attribute);
+// griddep_launch_dependents lets the next launch in the stream start its
+// CTAs (they run their own set-up, then block in their griddep_wait).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

@@ -364,6 +364,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   // EGD counter: the word after the abort flag (a static __shared__ variable
   // would come out of the 227 KB the dynamic allocation already claims)
   unsigned int* s_active = reinterpret_cast<unsigned int*>(const_cast<int*>(abort_flag) + 1);
+  // The tile masks (egd) and the activations come from earlier launches:
+  // read nothing of them before the dependency has resolved.
+  if (a.egd) griddep_wait();
   if (a.egd) {
     if (threadIdx.x == 0) *s_active = 0;
     __syncthreads();
@@ -394,6 +397,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Barrier set-up and the TMEM allocation above overlap the previous launch;
+  // everything below reads or writes tensors earlier launches produce or use.
+  if (!a.egd) griddep_wait();
+  griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const bool use_mask = !a.egd || *s_active <= a.egd_max_active;
 
@@ -951,6 +958,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
   // EGD counter: the word after the abort flag (a static __shared__ variable
   // would come out of the 227 KB the dynamic allocation already claims)
   unsigned int* s_active = reinterpret_cast<unsigned int*>(const_cast<int*>(abort_flag) + 1);
+  // The tile masks (egd) and the activations come from earlier launches:
+  // read nothing of them before the dependency has resolved.
+  if (a.egd) griddep_wait();
   if (a.egd) {
     if (threadIdx.x == 0) *s_active = 0;
     __syncthreads();
@@ -980,6 +990,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Barrier set-up and the TMEM allocation above overlap the previous launch;
+  // everything below reads or writes tensors earlier launches produce or use.
+  if (!a.egd) griddep_wait();
+  griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const bool use_mask = !a.egd || *s_active <= a.egd_max_active;
 
@@ -1247,6 +1261,27 @@ inline int allow_big_smem(const void* fn, std::atomic<bool>* done, const char* w
   return CF_OK;
 }
 
+// Launch with programmatic stream serialisation: the kernel's CTAs may start
+// while the previous launch in the stream drains (each kernel waits in
+// griddep_wait before touching tensors; inside a captured graph this becomes
+// a programmatic dependency edge).
+template <typename K>
+int launch_pdl(K kernel, int grid, int threads, int smem, cudaStream_t stream,
+               const CUtensorMap& t0, const CUtensorMap& t1, const ConvArgs& args,
+               const char* what) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, t0, t1, args), what);
+}
+
 template <int TP, int RES, bool FAST>
 int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, int grid,
                 cudaStream_t stream) {
@@ -1270,8 +1305,8 @@ int launch_inst(const CUtensorMap& tmA, const CUtensorMap& tmB, ConvArgs args, i
   if (int rc = allow_big_smem(reinterpret_cast<const void*>(conv_bn_lif_kernel<TP, RES, FAST>),
                               attr_done, "cudaFuncSetAttribute(conv)"))
     return rc;
-  conv_bn_lif_kernel<TP, RES, FAST><<<grid, kConvThreads, smem, stream>>>(tmA, tmB, args);
-  return check_launch("conv_bn_lif launch");
+  return launch_pdl(conv_bn_lif_kernel<TP, RES, FAST>, grid, kConvThreads, smem, stream, tmA,
+                    tmB, args, "conv_bn_lif launch");
 }
 
 template <int TP, int RES, bool FAST, int PL>
@@ -1294,8 +1329,8 @@ int launch_t(const CUtensorMap& tmX, const CUtensorMap& tmW, ConvArgs args, int 
   if (int rc = allow_big_smem(reinterpret_cast<const void*>(conv_t_kernel<TP, RES, FAST, PL>),
                               attr_done, "cudaFuncSetAttribute(conv_t)"))
     return rc;
-  conv_t_kernel<TP, RES, FAST, PL><<<grid, kTThreads, smem, stream>>>(tmX, tmW, args);
-  return check_launch("conv_t launch");
+  return launch_pdl(conv_t_kernel<TP, RES, FAST, PL>, grid, kTThreads, smem, stream, tmX, tmW,
+                    args, "conv_t launch");
 }
 
 template <int TP, int RES, bool FAST>
