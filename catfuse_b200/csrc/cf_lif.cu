@@ -87,8 +87,20 @@ __device__ __forceinline__ void store1(void* out, int fmt, int64_t idx, float s)
   else static_cast<uint8_t*>(out)[idx] = (uint8_t)s;
 }
 
+// Channel of neuron n in [B][C][HW]: 32-bit division when the sizes allow it
+// (a 64-bit division by a runtime value costs several times more).
+__device__ __forceinline__ int64_t channel_of(const LifArgs& a, int64_t n) {
+  if (a.N <= 0xFFFFFFFFll)
+    return (int64_t)(((uint32_t)n / (uint32_t)a.HW) % (uint32_t)a.C);
+  return (n / a.HW) % a.C;
+}
+
+// For Z_AFFINE, sc / sh are the BN scale and shift of the 4 neurons' channel
+// (HW % 4 == 0 on this path: they share one channel), looked up once per
+// neuron group by the caller.
 template <int MODE>
-__device__ __forceinline__ float4 zprime4(const LifArgs& a, int64_t t, int64_t n) {
+__device__ __forceinline__ float4 zprime4(const LifArgs& a, int64_t t, int64_t n, float sc,
+                                          float sh) {
   const int64_t i = t * a.N + n;
   float4 z;
   if (MODE == Z_ADD2) {
@@ -99,10 +111,6 @@ __device__ __forceinline__ float4 zprime4(const LifArgs& a, int64_t t, int64_t n
   } else {
     z = a.z ? load4(a.z, a.zfmt, i) : make_float4(0.f, 0.f, 0.f, 0.f);
     if (MODE == Z_AFFINE) {
-      // HW % 4 == 0 on this path: the 4 neurons share one channel.
-      const int64_t c = (n / a.HW) % a.C;
-      const float sc = a.scale ? __ldg(a.scale + c) : 1.f;
-      const float sh = a.shift ? __ldg(a.shift + c) : 0.f;
       if (a.z) {
         z.x = __fadd_rn(__fmul_rn(z.x, sc), sh);
         z.y = __fadd_rn(__fmul_rn(z.y, sc), sh);
@@ -154,12 +162,18 @@ __global__ void __launch_bounds__(kThreads) lif_vec_kernel(LifArgs a) {
     const int64_t g = wbase + (threadIdx.x & 31);
     const bool valid = g < ngroups;
     const int64_t n = (valid ? g : 0) << 2;
+    float sc = 1.f, sh = 0.f;
+    if (MODE == Z_AFFINE && valid) {
+      const int64_t c = channel_of(a, n);
+      if (a.scale) sc = __ldg(a.scale + c);
+      if (a.shift) sh = __ldg(a.shift + c);
+    }
     float4 v = (a.v0 && valid) ? *reinterpret_cast<const float4*>(a.v0 + n)
                                : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 znext = valid ? zprime4<MODE>(a, 0, n) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 znext = valid ? zprime4<MODE>(a, 0, n, sc, sh) : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int64_t t = 0; t < a.T; ++t) {
       const float4 z = znext;
-      if (t + 1 < a.T && valid) znext = zprime4<MODE>(a, t + 1, n);
+      if (t + 1 < a.T && valid) znext = zprime4<MODE>(a, t + 1, n, sc, sh);
       const float s0 = lif_step(v.x, z.x, a.lp);
       const float s1 = lif_step(v.y, z.y, a.lp);
       const float s2 = lif_step(v.z, z.z, a.lp);
@@ -167,6 +181,77 @@ __global__ void __launch_bounds__(kThreads) lif_vec_kernel(LifArgs a) {
       store4(a.spikes, a.sfmt, t * a.N + n, s0, s1, s2, s3, valid);
     }
     if (a.vT && valid) *reinterpret_cast<float4*>(a.vT + n) = v;
+  }
+}
+
+// Store 8 spikes of neurons [i, i+8) at step t (fp32 / fp16 / u8 formats):
+// one 16-byte store for fp16, where the 4-neuron path issues 8-byte ones.
+__device__ __forceinline__ void store8(void* out, int fmt, int64_t idx, const float (&sp)[8]) {
+  if (fmt == CF_FMT_F32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + idx);
+    __stcs(o, make_float4(sp[0], sp[1], sp[2], sp[3]));
+    __stcs(o + 1, make_float4(sp[4], sp[5], sp[6], sp[7]));
+  } else if (fmt == CF_FMT_F16) {
+    // spikes are 0 or 1: select the fp16 bit patterns
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[k] = (sp[2 * k] != 0.f ? 0x3C00u : 0u) | (sp[2 * k + 1] != 0.f ? 0x3C000000u : 0u);
+    __stcs(reinterpret_cast<uint4*>(static_cast<__half*>(out) + idx),
+           make_uint4(w[0], w[1], w[2], w[3]));
+  } else {  // U8
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      lo |= (uint32_t)sp[k] << (8 * k);
+      hi |= (uint32_t)sp[4 + k] << (8 * k);
+    }
+    __stcs(reinterpret_cast<uint2*>(static_cast<uint8_t*>(out) + idx), make_uint2(lo, hi));
+  }
+}
+
+// Vector path with 8 neurons per thread (N % 8 == 0, HW % 8 == 0 for the
+// affine mode, spikes not bit-packed): two 16-byte z loads per step and
+// 16-byte fp16 spike stores.
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) lif_vec8_kernel(LifArgs a) {
+  const int64_t ngroups = a.N >> 3;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < ngroups; g += stride) {
+    const int64_t n = g << 3;
+    float sc = 1.f, sh = 0.f;
+    if (MODE == Z_AFFINE) {
+      const int64_t c = channel_of(a, n);
+      if (a.scale) sc = __ldg(a.scale + c);
+      if (a.shift) sh = __ldg(a.shift + c);
+    }
+    float v[8];
+    if (a.v0) {
+      const float4 v0a = *reinterpret_cast<const float4*>(a.v0 + n);
+      const float4 v0b = *reinterpret_cast<const float4*>(a.v0 + n + 4);
+      v[0] = v0a.x; v[1] = v0a.y; v[2] = v0a.z; v[3] = v0a.w;
+      v[4] = v0b.x; v[5] = v0b.y; v[6] = v0b.z; v[7] = v0b.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = 0.f;
+    }
+    float4 na = zprime4<MODE>(a, 0, n, sc, sh), nb = zprime4<MODE>(a, 0, n + 4, sc, sh);
+    for (int64_t t = 0; t < a.T; ++t) {
+      const float z[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
+      if (t + 1 < a.T) {
+        na = zprime4<MODE>(a, t + 1, n, sc, sh);
+        nb = zprime4<MODE>(a, t + 1, n + 4, sc, sh);
+      }
+      float sp[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sp[k] = lif_step(v[k], z[k], a.lp);
+      store8(a.spikes, a.sfmt, t * a.N + n, sp);
+    }
+    if (a.vT) {
+      float4* o = reinterpret_cast<float4*>(a.vT + n);
+      o[0] = make_float4(v[0], v[1], v[2], v[3]);
+      o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
   }
 }
 
@@ -218,7 +303,16 @@ int launch_lif(LifArgs& a, int mode, cudaStream_t stream) {
     if (a.N % 32 != 0) return fail(CF_ERR_UNSUPPORTED, "bit-packed spikes need N %% 32 == 0");
     if (!vec) return fail(CF_ERR_UNSUPPORTED, "bit-packed spikes need 16-byte aligned inputs");
   }
-  if (vec) {
+  const bool vec8 = vec && a.sfmt != CF_FMT_BITS && a.N % 8 == 0 &&
+                    (mode != Z_AFFINE || a.HW % 8 == 0);
+  if (vec8) {
+    const int grid = grid_for(a.N / 8);
+    switch (mode) {
+      case Z_PLAIN: lif_vec8_kernel<Z_PLAIN><<<grid, kThreads, 0, stream>>>(a); break;
+      case Z_AFFINE: lif_vec8_kernel<Z_AFFINE><<<grid, kThreads, 0, stream>>>(a); break;
+      default: lif_vec8_kernel<Z_ADD2><<<grid, kThreads, 0, stream>>>(a); break;
+    }
+  } else if (vec) {
     const int grid = grid_for(a.N / 4);
     switch (mode) {
       case Z_PLAIN: lif_vec_kernel<Z_PLAIN><<<grid, kThreads, 0, stream>>>(a); break;

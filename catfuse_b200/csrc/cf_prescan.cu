@@ -43,16 +43,24 @@ constexpr int kRefChannelsPerCta = 32;
 __global__ void __launch_bounds__(kPrescanThreads)
     prescan_ref_kernel(const void* __restrict__ x, int fmt, int32_t* __restrict__ ag_mask,
                        int64_t* nnz, int C, int H, int W, int H_out, int W_out, int k, int s,
-                       int p, int BH, int BW, int GS, int GH, int GW, float thr) {
+                       int p, int BH, int BW, int GS, int GH, int GW, float thr, int sep) {
   extern __shared__ uint32_t s_tiles[];           // GH * GW masks of this sample
   uint16_t* s_row = reinterpret_cast<uint16_t*>(s_tiles + GH * GW);  // (first tile, count)
   uint16_t* s_col = s_row + 2 * H;
+  // Separable mode (small planes): every pixel's group bits land in s_pix,
+  // then the tile masks are OR-reduced from it along rows (s_cor[ih][tc]) and
+  // then along columns, instead of every pixel OR-ing into the shared masks of
+  // all its tiles (which piles same-address atomics onto a few words).
+  uint32_t* s_pix = reinterpret_cast<uint32_t*>(s_col + 2 * W);  // H * W
+  uint32_t* s_cor = s_pix + H * W;                                // H * GW
   __shared__ unsigned long long s_cnt;
   const int n_cb = (C + kRefChannelsPerCta - 1) / kRefChannelsPerCta;
   const int n = blockIdx.x / n_cb;
   const int cb = blockIdx.x - n * n_cb;
   const int c0 = cb * kRefChannelsPerCta, c1 = min(C, c0 + kRefChannelsPerCta);
   for (int i = threadIdx.x; i < GH * GW; i += blockDim.x) s_tiles[i] = 0;
+  if (sep)
+    for (int i = threadIdx.x; i < H * W; i += blockDim.x) s_pix[i] = 0;
   if (threadIdx.x == 0) s_cnt = 0;
   // input row ih feeds output rows o with o*s in [ih + p - k + 1, ih + p],
   // o < H_out; tile rows o / BH of that range
@@ -160,6 +168,11 @@ __global__ void __launch_bounds__(kPrescanThreads)
       }
     }
     fold();
+    if (sep) {
+      for (int j = 0; j < npx; ++j)
+        if (bits[j]) atomicOr(&s_pix[px0 + j], bits[j]);
+      continue;
+    }
     for (int j = 0; j < npx; ++j) {
       if (!bits[j]) continue;
       const int pix = px0 + j;
@@ -176,8 +189,36 @@ __global__ void __launch_bounds__(kPrescanThreads)
   }
   __syncthreads();
   int32_t* dst = ag_mask + (int64_t)n * GH * GW;
-  for (int i = threadIdx.x; i < GH * GW; i += blockDim.x)
-    if (s_tiles[i]) atomicOr(reinterpret_cast<unsigned int*>(dst + i), s_tiles[i]);
+  if (sep) {
+    // rows: s_cor[ih][tc] = OR of the pixels of row ih that feed tile column tc
+    for (int i = threadIdx.x; i < H * GW; i += blockDim.x) {
+      const int ih = i / GW, tc = i - (i / GW) * GW;
+      const int o_lo = tc * BW, o_hi = min(W_out - 1, o_lo + BW - 1);
+      const int lo = max(0, o_lo * s - p), hi = min(W - 1, o_hi * s - p + k - 1);
+      uint32_t acc = 0;
+      for (int iw = lo; iw <= hi; ++iw) {
+        const int f = s_col[2 * iw], c = s_col[2 * iw + 1];
+        if (tc >= f && tc < f + c) acc |= s_pix[ih * W + iw];
+      }
+      s_cor[i] = acc;
+    }
+    __syncthreads();
+    // columns: tile (th, tc) = OR of s_cor over the input rows feeding tile row th
+    for (int i = threadIdx.x; i < GH * GW; i += blockDim.x) {
+      const int th = i / GW, tc = i - (i / GW) * GW;
+      const int o_lo = th * BH, o_hi = min(H_out - 1, o_lo + BH - 1);
+      const int lo = max(0, o_lo * s - p), hi = min(H - 1, o_hi * s - p + k - 1);
+      uint32_t acc = 0;
+      for (int ih = lo; ih <= hi; ++ih) {
+        const int f = s_row[2 * ih], c = s_row[2 * ih + 1];
+        if (th >= f && th < f + c) acc |= s_cor[ih * GW + tc];
+      }
+      if (acc) atomicOr(reinterpret_cast<unsigned int*>(dst + i), acc);
+    }
+  } else {
+    for (int i = threadIdx.x; i < GH * GW; i += blockDim.x)
+      if (s_tiles[i]) atomicOr(reinterpret_cast<unsigned int*>(dst + i), s_tiles[i]);
+  }
   if (threadIdx.x == 0 && count && s_cnt)
     atomicAdd(reinterpret_cast<unsigned long long*>(nnz), s_cnt);
 }
@@ -203,6 +244,7 @@ __global__ void prescan_classify_kernel(const int32_t* __restrict__ ag_mask,
 constexpr int kMaxMapSide = 1024;  // H, W limits of the row / column tables
 constexpr int kMaxVpp = 1024;      // vector slots per pixel with a precomputed chunk bit
 constexpr int kMaxBandTiles = 2048;
+constexpr int kMaxBandPix = 5120;  // pixels of a band with separate chunk bits (R * W)
 
 __global__ void __launch_bounds__(kPrescanThreads)
     prescan_conv_kernel(const __half* __restrict__ x, uint32_t* __restrict__ mask,
@@ -212,6 +254,11 @@ __global__ void __launch_bounds__(kPrescanThreads)
   __shared__ uint32_t s_m[kMaxBandTiles];          // masks of the band's tile rows
   __shared__ uint16_t s_row[2 * kMaxMapSide], s_col[2 * kMaxMapSide];  // (first tile, count)
   __shared__ uint32_t s_cbit[kMaxVpp];
+  // Separable mode: each band pixel's chunk bits (s_pix) are collected first
+  // and every tile mask is then OR-reduced from them by one thread, instead
+  // of each pixel OR-ing into the shared masks of all its tiles (same-address
+  // atomics from many warps).
+  __shared__ uint32_t s_pix[kMaxBandPix];
   __shared__ unsigned long long s_cnt;
   const int n_band = (H + R - 1) / R;
   const int b = blockIdx.x / n_band;
@@ -251,7 +298,12 @@ __global__ void __launch_bounds__(kPrescanThreads)
     }
   }
   const int n_th = th_hi >= th_lo ? th_hi - th_lo + 1 : 0;
-  for (int i = threadIdx.x; i < n_th * n_wt; i += blockDim.x) s_m[i] = 0;
+  const bool sep = (r1 - r0) * W <= kMaxBandPix;
+  if (sep) {
+    for (int i = threadIdx.x; i < (r1 - r0) * W; i += blockDim.x) s_pix[i] = 0;
+  } else {
+    for (int i = threadIdx.x; i < n_th * n_wt; i += blockDim.x) s_m[i] = 0;
+  }
   __syncthreads();
   const bool count = nnz != nullptr;
   unsigned long long cnt = 0;
@@ -262,6 +314,10 @@ __global__ void __launch_bounds__(kPrescanThreads)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   // OR `bits` into the masks of every tile pixel (ih, col) feeds
   auto scatter = [&](int ih, int col, uint32_t bits) {
+    if (sep) {
+      atomicOr(&s_pix[(ih - r0) * W + col], bits);
+      return;
+    }
     const int tr0 = s_row[2 * ih], nr = s_row[2 * ih + 1];
     const int tc0 = s_col[2 * col], nc = s_col[2 * col + 1];
     for (int a = 0; a < nr; ++a)
@@ -348,7 +404,26 @@ __global__ void __launch_bounds__(kPrescanThreads)
   __syncthreads();
   const int bt = b / Bb;
   for (int i = threadIdx.x; i < n_th * n_wt; i += blockDim.x) {
-    const uint32_t mk = s_m[i];
+    uint32_t mk;
+    if (sep) {
+      // tile (th, tw): OR of the band pixels whose tables name it
+      const int th = th_lo + i / n_wt, tw = i - (i / n_wt) * n_wt;
+      const int oh_lo = th * Hb, oh_hi = min(Ho - 1, oh_lo + Hb - 1);
+      const int ow_lo = tw * Wb, ow_hi = min(Wo - 1, ow_lo + Wb - 1);
+      const int ih_lo = max(r0, oh_lo * s - p), ih_hi = min(r1 - 1, oh_hi * s - p + KH - 1);
+      const int iw_lo = max(0, ow_lo * s - p), iw_hi = min(W - 1, ow_hi * s - p + KW - 1);
+      mk = 0;
+      for (int ih = ih_lo; ih <= ih_hi; ++ih) {
+        const int f = s_row[2 * ih], c = s_row[2 * ih + 1];
+        if (th < f || th >= f + c) continue;
+        for (int iw = iw_lo; iw <= iw_hi; ++iw) {
+          const int fc = s_col[2 * iw], cc = s_col[2 * iw + 1];
+          if (tw >= fc && tw < fc + cc) mk |= s_pix[(ih - r0) * W + iw];
+        }
+      }
+    } else {
+      mk = s_m[i];
+    }
     if (!mk) continue;
     const int th = th_lo + i / n_wt, tw = i - (i / n_wt) * n_wt;
     atomicOr(mask + ((int64_t)bt * n_ht + th) * n_wt + tw, mk);
@@ -389,21 +464,28 @@ int cf_prescan(const void* x, int x_fmt, int32_t* ag_mask, int32_t* tile_class, 
                           "zero the masks"))
     return rc;
   const int n_cb = (int)((C + kRefChannelsPerCta - 1) / kRefChannelsPerCta);
-  const size_t smem = (size_t)GH * GW * 4 + (size_t)(H + W) * 4;
+  size_t smem = (size_t)GH * GW * 4 + (size_t)(H + W) * 4;
+  // separable tile reduction when the plane's pixel bits and the row partials
+  // fit 32 KB next to the masks (keeps several CTAs per SM)
+  const size_t sep_bytes = (size_t)(H * W + H * GW) * 4;
+  const int sep = sep_bytes <= 32 * 1024 ? 1 : 0;
+  if (sep) smem += sep_bytes;
+  if (smem > 200 * 1024) return fail(CF_ERR_UNSUPPORTED, "prescan tables exceed shared memory");
   static std::atomic<bool> attr_done[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr_done[dev].load()) {
+    // the attribute is a ceiling: raise it once to the largest size allowed above
     if (int rc = check_cuda(cudaFuncSetAttribute(prescan_ref_kernel,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem),
+                                                 200 * 1024),
                             "cudaFuncSetAttribute(prescan)"))
       return rc;
     attr_done[dev].store(true);
   }
   prescan_ref_kernel<<<(unsigned)(N * n_cb), kPrescanThreads, smem, s>>>(
       x, x_fmt, ag_mask, nnz_out, (int)C, (int)H, (int)W, (int)H_out, (int)W_out, (int)k,
-      (int)stride, (int)pad, (int)BH, (int)BW, (int)GS, (int)GH, (int)GW, threshold);
+      (int)stride, (int)pad, (int)BH, (int)BW, (int)GS, (int)GH, (int)GW, threshold, sep);
   if (int rc = check_launch("prescan launch")) return rc;
   int64_t blocks = (tiles + 255) / 256;
   if (blocks > 148 * 4) blocks = 148 * 4;

@@ -63,6 +63,124 @@ def _time(fn, reps, flush):
     return sum(a.elapsed_time(b) for a, b in ev) / reps * 1e3  # us
 
 
+def _time_stream(make, nbytes, reps, min_total=512 << 20):
+    """Steady-state device time (us per launch) of back-to-back launches:
+    ``make(i)`` returns the call for the i-th of k independent buffer sets,
+    k chosen so that the k sets together move more than ``min_total`` bytes
+    (four times the L2), so every launch streams its inputs from HBM without
+    an explicit flush.  The k launches are captured into one CUDA graph; the
+    replay is timed with CUDA events and divided by k, so the launch ramp and
+    the event clock's granularity are spread over k launches."""
+    k = max(2, -(-min_total // int(nbytes)))
+    fns = [make(i) for i in range(k)]
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / (reps * k), k
+
+
+def stream_table(dev, peak, src, reps):
+    """Back-to-back (steady-state) bandwidth of the memory-bound kernels at the
+    BASELINE shapes, beside a plain device copy of the same byte count."""
+    g = torch.Generator().manual_seed(1)
+    rows = []
+
+    def report(name, us, nbytes, k):
+        gbs = nbytes / us / 1e3
+        rows.append({"kernel": name, "us": us, "MB": nbytes / 1e6, "GBs": gbs,
+                     "frac": gbs / peak, "sets": k})
+        print(f"{name:58s} {us:8.1f} us {nbytes / 1e6:8.1f} MB {gbs:7.0f} GB/s "
+              f"{gbs / peak:6.1%} of {src} {peak:.0f}  (x{k} back to back)")
+
+    T, B, C, H, W = 4, 32, 128, 32, 32
+    N = B * C * H * W
+    zs, outs = {}, {}
+
+    def z_of(i):
+        if i not in zs:
+            zs[i] = (torch.randn(T, B, C, H, W, generator=g) * 0.8 + 0.3).to(dev)
+            outs[i] = torch.empty(T, B, C, H, W, dtype=torch.float16, device=dev)
+        return zs[i], outs[i]
+
+    nb = T * N * 4 + T * N * 2
+    # plain device copy of the same byte count (read z fp32 half, write half):
+    # the achievable streaming rate at this size
+    def mk_copy(i):
+        src_ = torch.empty(nb // 8, dtype=torch.float32, device=dev)
+        dst = torch.empty_like(src_)
+        return lambda: dst.copy_(src_)
+    us, k = _time_stream(mk_copy, nb, reps)
+    report("device copy (torch), same bytes as lif_fwd fp16", us, nb, k)
+
+    def mk_lif(i):
+        z, o = z_of(i)
+        return lambda: ops.lif_fwd(z, spike_dtype=torch.float16)
+    us, k = _time_stream(mk_lif, nb, reps)
+    report("lif_fwd  z fp32 -> spikes fp16  [4,32,128,32,32]", us, nb + 4 * N, k)
+    scale = torch.rand(C, generator=g).to(dev) + 0.5
+    shift = torch.randn(C, generator=g).to(dev) * 0.1
+
+    def mk_bn(i):
+        z, o = z_of(i)
+        return lambda: ops.bn_lif(z, scale, shift, spike_dtype=torch.float16)
+    us, k = _time_stream(mk_bn, nb, reps)
+    report("bn_lif   z fp32 -> spikes fp16", us, nb + 4 * N + 8 * C, k)
+    z2s = {}
+
+    def mk_add(i):
+        z, o = z_of(i)
+        if i not in z2s:
+            z2s[i] = torch.randn(T, B, C, H, W, generator=g).to(dev)
+        z2 = z2s[i]
+        return lambda: ops.add_lif(z, z2, spike_dtype=torch.float16)
+    us, k = _time_stream(mk_add, nb + T * N * 4, reps)
+    report("add_lif  2 x fp32 -> spikes fp16", us, nb + T * N * 4 + 4 * N, k)
+    zs.clear(); outs.clear(); z2s.clear()
+
+    T, B, C, H, W = 4, 32, 256, 28, 28
+    xs = {}
+
+    def x_of(i):
+        if i not in xs:
+            x = workloads.block_sparse_spikes(T, B, C, H, W, 0.9, seed=900 + i).to(dev)
+            xp = ops.pack_tbchw(x)
+            xr = x.reshape(T * B, C, H, W).half().contiguous()
+            del x
+            xs[i] = (xp, xr, ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1))
+        return xs[i]
+    xbytes = T * B * C * H * W * 2
+
+    def mk_pc(i):
+        xp, _, m = x_of(i)
+        return lambda: ops.prescan_conv_tiles(xp, C, 3, 3, 1, 1, mask_out=m)
+    us, k = _time_stream(mk_pc, xbytes, reps)
+    report("prescan_conv_tiles  x [32,28,28,4,256] fp16  s=0.9", us, xbytes, k)
+
+    def mk_pr(i):
+        _, xr, _ = x_of(i)
+        return lambda: ops.prescan(xr, 3, 1, 1, 8, 8, 32)
+    us, k = _time_stream(mk_pr, xbytes, reps)
+    report("prescan (reference geometry) x [128,256,28,28] fp16", us, xbytes, k)
+    print(json.dumps({"hbm_stream": rows, "peak_gbs": peak, "peak_source": src}))
+    return rows
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -70,9 +188,15 @@ def main(argv=None):
     ap.add_argument("--only", choices=["lif", "prescan", "sweep"], default=None,
                     help="run one group: the LIF family, the two prescans once each on the "
                          "config-2 input (s = 0.9), or the SparseFlow sweep")
+    ap.add_argument("--stream", action="store_true",
+                    help="steady-state table: each kernel launched back to back over buffer "
+                         "sets larger than L2 (no flush), beside a device copy of equal bytes")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
     peak, src = _peak()
+    if args.stream:
+        stream_table(dev, peak, src, args.reps)
+        return 0
     flush = L2Flush(dev)
     g = torch.Generator().manual_seed(0)
     rows = []
