@@ -239,6 +239,23 @@ int conv_bn_lif_impl(const void* x, const void* wp, const float* scale, const fl
   if (int rc = make_geometry(T, B, Ho, Wo, Cout, Cin_p, stride, tile_mask != nullptr && !egd_launch,
                              g, nplanes))
     return rc;
+  // Dense launches whose kh-box stage does not fit twice at BK = 64 take
+  // BK = 32 when that fits it at least three times: the stage then carries
+  // KH * 2 MMAs per barrier round trip and the activation rows serve every kh
+  // tap, 73 instead of 96 operand bytes per MMA cycle, i.e. about 30 % more
+  // MMA work buffered in the same shared memory (config-0 layer: -5 % time).
+  // Masked launches keep the mask's chunk.
+  if (!tile_mask && g.tmode && stride == 1 && KH > 1 && g.Bb == 1 && g.BK == 64 &&
+      (g.Wb * g.TP) % 16 == 0) {
+    auto khstage = [&](int64_t bk) {
+      return (int64_t)(g.Hb + KH - 1) * g.Wb * g.TP * bk * 2 + KH * (int64_t)g.BN * bk * 2;
+    };
+    if ((kTSmemBudget - kTFixedBytes) / khstage(64) < 2 &&
+        (kTSmemBudget - kTFixedBytes) / khstage(32) >= 3) {
+      g.BK = 32;
+      g.n_kc = (int)(Cin_p / 32);
+    }
+  }
   const int n_kx = g.n_kc;  // activation chunks per tap
   g.n_kc *= wparts;          // weight chunks: part 0 chunks, then part 1, ...
   if (tile_mask && g.n_kc > 32)

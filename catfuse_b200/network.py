@@ -388,6 +388,11 @@ class CTFNetwork(nn.Module):
     """Wraps a rewritten spiking ResNet; ``forward(x[T, B, C, H, W])`` runs the
     native plan and returns logits [T, B, classes] (fp32)."""
 
+    #: When true, every forward reads the device error word of the bounded
+    #: waits (one stream synchronisation) and raises CatfuseNativeError if a
+    #: wait expired; the test suite turns it on.
+    check_errors = False
+
     def __init__(self, model: nn.Module, use_graph: bool = True, use_sparse: bool = True,
                  precision: str = "fp16"):
         super().__init__()
@@ -430,4 +435,8 @@ class CTFNetwork(nn.Module):
             p.fresh = True
             self._fresh = False
         p.x_in.copy_(x)
-        return p.run(self.use_graph).clone()
+        out = p.run(self.use_graph).clone()
+        if self.check_errors:
+            # synchronises: raises if a bounded device wait expired in this forward
+            ops.check_device_error()
+        return out

@@ -345,6 +345,11 @@ class CTFSpikformer(nn.Module):
     """Wraps a rewritten Spikformer; ``forward(x[T, B, 3, H, W])`` runs the
     native plan and returns logits [T, B, classes] (fp32)."""
 
+    #: When true, every forward reads the device error word of the bounded
+    #: waits (one stream synchronisation) and raises CatfuseNativeError if a
+    #: wait expired; the test suite turns it on.
+    check_errors = False
+
     def __init__(self, model: nn.Module, use_graph: bool = True, precision: str = "fp16"):
         super().__init__()
         if not is_spikformer(model):
@@ -382,7 +387,11 @@ class CTFSpikformer(nn.Module):
             p.fresh = True
             self._fresh = False
         p.x_in.copy_(x)
-        return p.run(self.use_graph).clone()
+        out = p.run(self.use_graph).clone()
+        if self.check_errors:
+            # synchronises: raises if a bounded device wait expired in this forward
+            ops.check_device_error()
+        return out
 
 
 __all__ = ["SpikformerPlan", "CTFSpikformer", "is_spikformer", "UnsupportedSpikformer"]

@@ -36,3 +36,20 @@ def dev():
     from catfuse_b200 import _lib
     _lib.load()
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _device_error_word(request):
+    """GPU tests run with the networks' per-forward error check on, and after
+    each one the bounded-wait error word must be clear (an expired wait would
+    otherwise leave wrong tensors without an exception)."""
+    if request.node.get_closest_marker("gpu") is None or not cuda_ok():
+        yield
+        return
+    from catfuse_b200 import ops
+    from catfuse_b200.network import CTFNetwork
+    from catfuse_b200.spikformer_net import CTFSpikformer
+    CTFNetwork.check_errors = True
+    CTFSpikformer.check_errors = True
+    yield
+    ops.check_device_error()
